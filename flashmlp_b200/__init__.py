@@ -1,0 +1,22 @@
+"""flashmlp_b200 — B200 (sm_100a) fused multi-head MLP, a drop-in for dtadpole/flashMLP.
+
+Public names match the reference module `flashmlp` (flashmlp.py): flashmlp_fwd,
+flashmlp_bwd, FlashMLPFunction, FlashMLP, plus the plain-PyTorch PyTorchMLP,
+flashmlp_torch_fwd and flashmlp_torch_bwd it also exports. Multi-GPU wrappers live in
+flashmlp_b200.sharding.
+"""
+from .api import FlashMLP, FlashMLPFunction, activation_code, flashmlp_bwd, flashmlp_fwd
+from .torch_reference import PyTorchMLP, flashmlp_torch_bwd, flashmlp_torch_fwd
+from ._lib import FlashMLPError
+
+__all__ = [
+    "flashmlp_fwd",
+    "flashmlp_bwd",
+    "FlashMLPFunction",
+    "FlashMLP",
+    "PyTorchMLP",
+    "flashmlp_torch_fwd",
+    "flashmlp_torch_bwd",
+    "FlashMLPError",
+    "activation_code",
+]

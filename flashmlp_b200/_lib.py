@@ -1,0 +1,76 @@
+"""ctypes binding of libflashmlp_b200.so (declared in include/flashmlp_b200.h).
+
+The shared library is the only compute path: if it is missing this module raises, there
+is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libflashmlp_b200.so")
+
+FMLP_DTYPE_F16 = 0
+FMLP_DTYPE_BF16 = 1
+
+FMLP_ACT_LINEAR = 0
+FMLP_ACT_LEAKY_RELU = 1
+FMLP_ACT_SILU = 2
+FMLP_ACT_SIGMOID = 3
+
+FMLP_OK = 0
+FMLP_ERR_UNSUPPORTED_D = 3
+FMLP_ERR_UNSUPPORTED_E = 4
+FMLP_ERR_DEVICE_TIMEOUT = 10
+
+# Every symbol the header declares, with (restype, argtypes).
+_c_int, _c_vp, _c_sz = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
+SIGNATURES = {
+    "fmlp_fwd": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp]),
+    "fmlp_bwd": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_sz,
+         _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp],
+    ),
+    "fmlp_bwd_workspace_size": (_c_sz, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "fmlp_sgd_update": (_c_int, [_c_vp, _c_vp, ctypes.c_longlong, ctypes.c_float, _c_int, _c_vp]),
+    "fmlp_device_status": (_c_int, [_c_int]),
+    "fmlp_error_string": (ctypes.c_char_p, [_c_int]),
+    "fmlp_abi_version": (_c_int, []),
+}
+
+_LIB = None
+
+
+class FlashMLPError(RuntimeError):
+    """A non-zero return code from the C ABI."""
+
+    def __init__(self, code: int, where: str):
+        self.code = code
+        super().__init__(f"{where}: {error_string(code)} (code {code})")
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH.name} is not built; run `python -m flashmlp_b200.build` "
+                "(there is no non-CUDA fallback)"
+            )
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = handle
+    return _LIB
+
+
+def error_string(code: int) -> str:
+    return lib().fmlp_error_string(code).decode()
+
+
+def check(code: int, where: str) -> None:
+    if code != FMLP_OK:
+        raise FlashMLPError(code, where)

@@ -1,0 +1,189 @@
+"""Python surface of the fused multi-head MLP, call-compatible with dtadpole/flashMLP.
+
+    Z = X @ W1,  H = act(Z),  O = H @ W2          per head
+    X: (H, B, D)   W1: (H, D, E)   W2: (H, E, D)   O: (H, B, D)
+
+`flashmlp_fwd`, `flashmlp_bwd`, `FlashMLPFunction` and `FlashMLP` keep the reference's
+names, signatures, shape assertions (and their messages) and return conventions
+(flashmlp.py:428-616). Their compute goes through libflashmlp_b200.so (hand-written
+sm_100a kernels); there is no other compute path.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Tuple
+
+import numpy as np
+import torch
+
+from . import _lib
+
+_ACT_CODES = {
+    "leaky_relu": _lib.FMLP_ACT_LEAKY_RELU,
+    "silu": _lib.FMLP_ACT_SILU,
+    "sigmoid": _lib.FMLP_ACT_SIGMOID,
+}
+
+
+def activation_code(activation: str) -> int:
+    """Maps an activation name to the C ABI code. Like the reference, any other string
+    (including "") means no activation (flashmlp.py:146-147)."""
+    return _ACT_CODES.get(activation, _lib.FMLP_ACT_LINEAR)
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return _lib.FMLP_DTYPE_BF16
+    if t.dtype == torch.float16:
+        return _lib.FMLP_DTYPE_F16
+    raise TypeError(
+        f"flashmlp_b200 supports torch.bfloat16 and torch.float16 tensors, got {t.dtype}"
+    )
+
+
+def _check_tensors(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    if dev.type != "cuda":
+        raise RuntimeError("flashmlp_b200 kernels need CUDA tensors (there is no CPU path)")
+    for t in ts[1:]:
+        if t.device != dev:
+            raise RuntimeError(f"all tensors must be on {dev}, got one on {t.device}")
+        if t.dtype != ts[0].dtype:
+            raise TypeError(f"all tensors must share one dtype, got {ts[0].dtype} and {t.dtype}")
+    _dtype_code(ts[0])
+    return dev
+
+
+def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def flashmlp_fwd(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                 activation: str = "") -> torch.Tensor:
+    """Forward pass; drop-in for flashmlp.py:428-477.
+
+    Args:
+        x: (H, B, D); w1: (H, D, E); w2: (H, E, D); activation: "silu", "leaky_relu",
+        "sigmoid" or "" (anything else is linear).
+    Returns:
+        O of shape (H, B, D), same dtype as x.
+    """
+    assert x.shape[0] == w1.shape[0], "Number of heads must match"
+    assert x.shape[0] == w2.shape[0], "Number of heads must match"
+    assert x.shape[2] == w1.shape[1], "Hidden dimension mismatch"
+    assert w1.shape[2] == w2.shape[1], "Intermediate dimension mismatch"
+    assert x.shape[2] == w2.shape[2], "Output dimension mismatch"
+
+    H, B, D = x.shape
+    E = w1.shape[2]
+
+    x = x.reshape(H * B, D)
+    w1 = w1.reshape(D * H, E)
+    w2 = w2.reshape(E * H, D)
+
+    assert x.is_contiguous(), "Input X must be contiguous"
+    assert w1.is_contiguous(), "Weight W1 must be contiguous"
+    assert w2.is_contiguous(), "Weight W2 must be contiguous"
+
+    dev = _check_tensors(x, w1, w2)
+    o = torch.empty_like(x)
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = L.fmlp_fwd(_ptr(x), _ptr(w1), _ptr(w2), _ptr(o), H, B, D, E,
+                        _dtype_code(x), activation_code(activation), ctypes.c_void_p(stream))
+    _lib.check(rc, "fmlp_fwd")
+    return o.reshape(H, B, D)
+
+
+def flashmlp_bwd(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                 do: torch.Tensor, activation: str = "") -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Backward pass; drop-in for flashmlp.py:480-538. Recomputes Z and H from X, W1 and W2.
+
+    Returns:
+        (dx, dw1, dw2) with the shapes of (x, w1, w2).
+    """
+    assert x.shape[2] == w1.shape[1], "Hidden dimension mismatch"
+    assert w1.shape[2] == w2.shape[1], "Intermediate dimension mismatch"
+    assert x.shape[2] == w2.shape[2], "Output dimension mismatch"
+    assert x.shape == do.shape, "Gradient shape mismatch"
+
+    H, B, D = x.shape
+    E = w1.shape[2]
+
+    x = x.reshape(H * B, D)
+    w1 = w1.reshape(D * H, E)
+    w2 = w2.reshape(E * H, D)
+    do = do.reshape(H * B, D).contiguous()
+
+    assert x.is_contiguous(), "Input X must be contiguous"
+    assert w1.is_contiguous(), "Weight W1 must be contiguous"
+    assert w2.is_contiguous(), "Weight W2 must be contiguous"
+    assert do.is_contiguous(), "Gradient dO must be contiguous"
+
+    dev = _check_tensors(x, w1, w2, do)
+    dx = torch.empty_like(x)
+    dw1 = torch.empty_like(w1)
+    dw2 = torch.empty_like(w2)
+    L = _lib.lib()
+    dt = _dtype_code(x)
+    ws_bytes = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = L.fmlp_bwd(_ptr(x), _ptr(w1), _ptr(w2), _ptr(do), _ptr(dx), _ptr(dw1), _ptr(dw2),
+                        _ptr(ws) if ws is not None else None, ws_bytes, H, B, D, E, dt,
+                        activation_code(activation), ctypes.c_void_p(stream))
+    _lib.check(rc, "fmlp_bwd")
+    return dx.reshape(H, B, D), dw1.reshape(H, D, E), dw2.reshape(H, E, D)
+
+
+class FlashMLPFunction(torch.autograd.Function):
+    """Autograd wrapper; saves only X, W1 and W2 (flashmlp.py:545-557)."""
+
+    @staticmethod
+    def forward(ctx, x, w1, w2, activation=""):
+        o = flashmlp_fwd(x, w1, w2, activation)
+        ctx.save_for_backward(x, w1, w2)
+        ctx.activation = activation
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        x, w1, w2 = ctx.saved_tensors
+        dx, dw1, dw2 = flashmlp_bwd(x, w1, w2, do, ctx.activation)
+        return dx, dw1, dw2, None
+
+
+class FlashMLP(torch.nn.Module):
+    """Multi-head MLP module (flashmlp.py:564-616).
+
+    Parameters `w1` (H, D, E) and `w2` (H, E, D) are initialised like the reference,
+    randn / sqrt(E) and randn / sqrt(D), so state dicts interchange. A 2-D input (B, D) is
+    broadcast to every head and the output is averaged over heads.
+    """
+
+    def __init__(self, num_heads: int, hidden_dim: int, intermediate_dim: int,
+                 activation: str = "silu", dtype=torch.float16, device="cuda"):
+        super().__init__()
+        self.num_heads = num_heads
+        self.hidden_dim = hidden_dim
+        self.intermediate_dim = intermediate_dim
+        self.activation = activation
+        self.w1 = torch.nn.Parameter(
+            torch.randn(num_heads, hidden_dim, intermediate_dim, dtype=dtype, device=device)
+            / np.sqrt(intermediate_dim)
+        )
+        self.w2 = torch.nn.Parameter(
+            torch.randn(num_heads, intermediate_dim, hidden_dim, dtype=dtype, device=device)
+            / np.sqrt(hidden_dim)
+        )
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        squeeze_output = x.dim() == 2
+        if squeeze_output:
+            x = x.unsqueeze(0).expand(self.num_heads, -1, -1)
+        o = FlashMLPFunction.apply(x, self.w1, self.w2, self.activation)
+        if squeeze_output:
+            o = o.mean(dim=0)
+        return o

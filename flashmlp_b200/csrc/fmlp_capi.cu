@@ -1,0 +1,234 @@
+// C ABI of libflashmlp_b200.so: argument checks, TMA tensor maps, launches.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/flashmlp_b200.h"
+#include "fmlp_kernels.h"
+#include "fmlp_ptx.cuh"
+
+namespace fmlp {
+
+// Per-device kernel status word (see fmlp_ptx.cuh, mbar_wait).
+__device__ uint32_t g_fmlp_status;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  bool init = false;
+  int sm_count = 0;
+  int cc_major = 0;
+  uint32_t* status = nullptr;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FMLP_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.init) {
+    if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return FMLP_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return FMLP_ERR_CUDA;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fmlp_status) != cudaSuccess) return FMLP_ERR_CUDA;
+    d.status = static_cast<uint32_t*>(p);
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+              cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || fn == nullptr)
+        return FMLP_ERR_TMA;
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    d.init = true;
+  }
+  if (d.cc_major != 10) return FMLP_ERR_DEVICE;
+  *out = &d;
+  return FMLP_OK;
+}
+
+// 3-D tiled map over a contiguous (d2, d1, d0) row-major tensor of 16-bit elements,
+// 128-byte swizzle, zero fill out of bounds.
+int encode3d(CUtensorMap* m, const void* ptr, int bf16, uint64_t d0, uint64_t d1, uint64_t d2,
+             uint32_t b0, uint32_t b1) {
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        3, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FMLP_OK : FMLP_ERR_TMA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_common(int H, int B, int D, int E, int dtype) {
+  if (H < 0 || B < 0 || D < 0 || E < 0) return FMLP_ERR_INVALID_SHAPE;
+  if (dtype != FMLP_DTYPE_F16 && dtype != FMLP_DTYPE_BF16) return FMLP_ERR_UNSUPPORTED_DTYPE;
+  const long long hb = (long long)H * B, hd = (long long)H * D;
+  if (hb * D >= (1LL << 40) || hd * E >= (1LL << 40)) return FMLP_ERR_INVALID_SHAPE;
+  if (B > (1 << 30) || E > (1 << 30)) return FMLP_ERR_INVALID_SHAPE;
+  return FMLP_OK;
+}
+
+int round_dp(int D) { return D <= 64 ? 64 : (D <= 128 ? 128 : 256); }
+
+int cuda_rc(cudaError_t e) { return e == cudaSuccess ? FMLP_OK : FMLP_ERR_CUDA; }
+
+__global__ void sgd_kernel_bf16(__nv_bfloat16* w, const float* g, long long n, float lr) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    w[i] = __float2bfloat16_rn(__bfloat162float(w[i]) - lr * g[i]);
+}
+__global__ void sgd_kernel_f16(__half* w, const float* g, long long n, float lr) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    w[i] = __float2half_rn(__half2float(w[i]) - lr * g[i]);
+}
+
+}  // namespace
+}  // namespace fmlp
+
+using namespace fmlp;
+
+extern "C" {
+
+int fmlp_abi_version(void) { return 100; }
+
+const char* fmlp_error_string(int code) {
+  switch (code) {
+    case FMLP_OK: return "ok";
+    case FMLP_ERR_INVALID_SHAPE: return "invalid shape (negative size or too large)";
+    case FMLP_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype (only float16 and bfloat16)";
+    case FMLP_ERR_UNSUPPORTED_D:
+      return "unsupported hidden dim D (needs D % 16 == 0, D <= 256 forward, D <= 128 backward)";
+    case FMLP_ERR_UNSUPPORTED_E: return "unsupported intermediate dim E (needs E % 8 == 0)";
+    case FMLP_ERR_MISALIGNED: return "tensor data pointer is not 16-byte aligned";
+    case FMLP_ERR_CUDA: return "CUDA runtime error";
+    case FMLP_ERR_TMA: return "TMA tensor-map encoding failed";
+    case FMLP_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    case FMLP_ERR_WORKSPACE: return "workspace too small";
+    case FMLP_ERR_DEVICE_TIMEOUT: return "a kernel pipeline wait timed out on the device";
+  }
+  return "unknown error";
+}
+
+int fmlp_fwd(const void* x, const void* w1, const void* w2, void* o, int H, int B, int D, int E,
+             int dtype, int act, void* stream) {
+  int rc = check_common(H, B, D, E, dtype);
+  if (rc) return rc;
+  if (D % 16 != 0 || D > 256) return FMLP_ERR_UNSUPPORTED_D;
+  if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((long long)H * B * D == 0) return FMLP_OK;
+  if (E == 0) return cuda_rc(cudaMemsetAsync(o, 0, size_t(H) * B * D * 2, st));
+  if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(o)) return FMLP_ERR_MISALIGNED;
+  FwdLaunch a{};
+  a.dp = round_dp(D);
+  const int et = fwd_et(a.dp);
+  const int bf = dtype == FMLP_DTYPE_BF16;
+  if ((rc = encode3d(&a.tm_x, x, bf, D, B, H, 64, kRows))) return rc;
+  if ((rc = encode3d(&a.tm_w1, w1, bf, E, D, H, 64, a.dp))) return rc;
+  if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, et))) return rc;
+  a.o = o;
+  a.H = H, a.B = B, a.D = D, a.E = E;
+  a.bf16 = bf;
+  a.act = act;
+  const long long tiles = (long long)H * ((B + kRows - 1) / kRows);
+  a.grid = int(tiles < dev->sm_count ? tiles : dev->sm_count);
+  a.status = dev->status;
+  a.stream = st;
+  return cuda_rc(launch_fwd(a));
+}
+
+size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {
+  (void)H, (void)B, (void)D, (void)E, (void)dtype;
+  return 0;
+}
+
+int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1,
+             void* dw2, void* workspace, size_t workspace_bytes, int H, int B, int D, int E,
+             int dtype, int act, void* stream) {
+  (void)workspace;
+  int rc = check_common(H, B, D, E, dtype);
+  if (rc) return rc;
+  if (D % 16 != 0 || D > 128) return FMLP_ERR_UNSUPPORTED_D;
+  if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
+  if (workspace_bytes < fmlp_bwd_workspace_size(H, B, D, E, dtype)) return FMLP_ERR_WORKSPACE;
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (H == 0 || D == 0) return FMLP_OK;
+  if (E == 0) return cuda_rc(cudaMemsetAsync(dx, 0, size_t(H) * B * D * 2, st));
+  if (B == 0) {
+    if ((rc = cuda_rc(cudaMemsetAsync(dw1, 0, size_t(H) * D * E * 2, st)))) return rc;
+    return cuda_rc(cudaMemsetAsync(dw2, 0, size_t(H) * E * D * 2, st));
+  }
+  if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(dO) || !aligned16(dx) ||
+      !aligned16(dw1) || !aligned16(dw2))
+    return FMLP_ERR_MISALIGNED;
+  BwdLaunch a{};
+  a.dp = round_dp(D);
+  const int bf = dtype == FMLP_DTYPE_BF16;
+  if ((rc = encode3d(&a.tm_x, x, bf, D, B, H, 64, kRows))) return rc;
+  if ((rc = encode3d(&a.tm_do, dO, bf, D, B, H, 64, kRows))) return rc;
+  if ((rc = encode3d(&a.tm_w1, w1, bf, E, D, H, 64, a.dp))) return rc;
+  if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, kBwdEtX))) return rc;
+  if ((rc = encode3d(&a.tm_w2w, w2, bf, D, E, H, 64, kBwdEtW))) return rc;
+  a.dx = dx, a.dw1 = dw1, a.dw2 = dw2;
+  a.H = H, a.B = B, a.D = D, a.E = E;
+  a.bf16 = bf;
+  a.act = act;
+  a.status = dev->status;
+  a.stream = st;
+  return cuda_rc(launch_bwd(a));
+}
+
+int fmlp_sgd_update(void* w, const float* g, long long n, float lr, int dtype, void* stream) {
+  if (n < 0) return FMLP_ERR_INVALID_SHAPE;
+  if (dtype != FMLP_DTYPE_F16 && dtype != FMLP_DTYPE_BF16) return FMLP_ERR_UNSUPPORTED_DTYPE;
+  DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  if (n == 0) return FMLP_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  long long blocks = (n + 255) / 256;
+  const long long cap = (long long)dev->sm_count * 8;
+  if (blocks > cap) blocks = cap;
+  if (dtype == FMLP_DTYPE_BF16)
+    sgd_kernel_bf16<<<unsigned(blocks), 256, 0, st>>>(static_cast<__nv_bfloat16*>(w), g, n, lr);
+  else
+    sgd_kernel_f16<<<unsigned(blocks), 256, 0, st>>>(static_cast<__half*>(w), g, n, lr);
+  return cuda_rc(cudaGetLastError());
+}
+
+int fmlp_device_status(int reset) {
+  DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  if (cudaDeviceSynchronize() != cudaSuccess) return FMLP_ERR_CUDA;
+  uint32_t v = 0;
+  if (cudaMemcpy(&v, dev->status, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return FMLP_ERR_CUDA;
+  if (reset) {
+    const uint32_t z = 0;
+    if (cudaMemcpy(dev->status, &z, sizeof(z), cudaMemcpyHostToDevice) != cudaSuccess) return FMLP_ERR_CUDA;
+  }
+  return v ? FMLP_ERR_DEVICE_TIMEOUT : FMLP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,50 @@
+// Host-side launch interface shared by the kernel translation units and the C ABI.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace fmlp {
+
+struct FwdLaunch {
+  CUtensorMap tm_x;   // X  (H,B,D)  viewed 3-D {D, B, H}, box {64, 128, 1}
+  CUtensorMap tm_w1;  // W1 (H,D,E)  viewed 3-D {E, D, H}, box {64, DP, 1}
+  CUtensorMap tm_w2;  // W2 (H,E,D)  viewed 3-D {D, E, H}, box {64, ET, 1}
+  void* o;            // O  (H,B,D)  row-major, written directly
+  int H, B, D, E;
+  int dp;             // D rounded up to a multiple of 64 (64, 128 or 256)
+  int bf16;           // 1 = bfloat16, 0 = float16
+  int act;            // fmlp::Act
+  int grid;           // persistent CTAs
+  uint32_t* status;   // device status word
+  cudaStream_t stream;
+};
+
+struct BwdLaunch {
+  CUtensorMap tm_x;    // X  {D, B, H}, box {64, 128, 1}
+  CUtensorMap tm_do;   // dO {D, B, H}, box {64, 128, 1}
+  CUtensorMap tm_w1;   // W1 {E, D, H}, box {64, DP, 1}
+  CUtensorMap tm_w2;   // W2 {D, E, H}, box {64, 64, 1}   (64-row E chunks)
+  CUtensorMap tm_w2w;  // W2 {D, E, H}, box {64, 128, 1}  (128-row E chunks, dW programs)
+  void* dx;
+  void* dw1;
+  void* dw2;
+  int H, B, D, E;
+  int dp, bf16, act;
+  uint32_t* status;
+  cudaStream_t stream;
+};
+
+// Tile constants shared by host and device.
+constexpr int kRows = 128;  // rows of a B tile (tcgen05 M)
+
+inline int fwd_et(int dp) { return dp <= 128 ? 128 : 64; }
+constexpr int kBwdEtX = 64;   // E chunk of the dX programs
+constexpr int kBwdEtW = 128;  // E chunk owned by one dW program
+
+int fwd_smem_bytes(int dp);
+int bwd_smem_bytes(int dp);
+cudaError_t launch_fwd(const FwdLaunch& a);
+cudaError_t launch_bwd(const BwdLaunch& a);
+
+}  // namespace fmlp

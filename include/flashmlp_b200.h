@@ -1,0 +1,89 @@
+/*
+ * flashmlp_b200 — C ABI of the B200 (sm_100a) fused multi-head MLP.
+ *
+ *   O[h] = act(X[h] @ W1[h]) @ W2[h]          X, O: (H,B,D)  W1: (H,D,E)  W2: (H,E,D)
+ *
+ * These entry points are the drop-in boundary for the two Triton launches of the
+ * reference (dtadpole/flashMLP, flashmlp.py): every argument is a plain pointer or size,
+ * all pointers are DEVICE pointers to contiguous row-major tensors with exactly the
+ * reference's layouts, and the caller owns every allocation. Work is enqueued
+ * asynchronously on `stream` (a cudaStream_t; NULL = legacy default stream) of the
+ * current device. Every function returns 0 on success or one of the FMLP_ERR_* codes.
+ */
+#ifndef FLASHMLP_B200_H_
+#define FLASHMLP_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+#define FMLP_DTYPE_F16 0
+#define FMLP_DTYPE_BF16 1
+
+/* activation codes; the reference treats any unknown activation string as linear
+ * (flashmlp.py:146-147, :682-683) and so does the Python layer of this library. */
+#define FMLP_ACT_LINEAR 0
+#define FMLP_ACT_LEAKY_RELU 1 /* slope 0.01, z >= 0 takes the identity branch */
+#define FMLP_ACT_SILU 2
+#define FMLP_ACT_SIGMOID 3
+
+/* error codes */
+#define FMLP_OK 0
+#define FMLP_ERR_INVALID_SHAPE 1    /* negative size or size overflow                  */
+#define FMLP_ERR_UNSUPPORTED_DTYPE 2 /* only fp16 and bf16                             */
+#define FMLP_ERR_UNSUPPORTED_D 3    /* D % 16 != 0, or D > 256 (fwd) / D > 128 (bwd)    */
+#define FMLP_ERR_UNSUPPORTED_E 4    /* E % 8 != 0 (row stride of W1 must be 16 bytes)  */
+#define FMLP_ERR_MISALIGNED 5       /* a pointer is not 16-byte aligned                */
+#define FMLP_ERR_CUDA 6             /* CUDA runtime / launch error                     */
+#define FMLP_ERR_TMA 7              /* tensor-map encoding failed                      */
+#define FMLP_ERR_DEVICE 8           /* current device is not an sm_100 (B200) GPU       */
+#define FMLP_ERR_WORKSPACE 9        /* workspace smaller than fmlp_bwd_workspace_size  */
+#define FMLP_ERR_DEVICE_TIMEOUT 10  /* a kernel's bounded pipeline wait ran out        */
+
+/*
+ * Forward. Replaces flashmlp_fwd + flashmlp_fwd_kernel (flashmlp.py:428-477, :63-158).
+ * o (H,B,D) is fully written (the reference zero-fills it first, flashmlp.py:462).
+ */
+int fmlp_fwd(const void* x, const void* w1, const void* w2, void* o, int H, int B, int D, int E,
+             int dtype, int act, void* stream);
+
+/*
+ * Unified backward. Replaces flashmlp_bwd + flashmlp_bwd_kernel (flashmlp.py:480-538,
+ * :341-421). dO must be contiguous (the reference makes it so, flashmlp.py:508).
+ * dx (H,B,D), dw1 (H,D,E) and dw2 (H,E,D) are fully written. `workspace` is device
+ * scratch of at least fmlp_bwd_workspace_size(...) bytes (may be NULL when that is 0).
+ */
+int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1,
+             void* dw2, void* workspace, size_t workspace_bytes, int H, int B, int D, int E,
+             int dtype, int act, void* stream);
+
+/* Device scratch bytes fmlp_bwd needs for this shape (no reference counterpart; the
+ * reference allocates its outputs with torch.zeros_like, flashmlp.py:516-518). */
+size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype);
+
+/*
+ * In-place SGD step w[i] -= lr * g[i] for n elements, g in fp32 (e.g. the all-reduced
+ * sum of dW shards) and w in `dtype`. Used by the batch-sharded multi-GPU training step;
+ * the reference has no optimizer (no counterpart).
+ */
+int fmlp_sgd_update(void* w, const float* g, long long n, float lr, int dtype, void* stream);
+
+/* Reads the current device's kernel status word (FMLP_OK or FMLP_ERR_DEVICE_TIMEOUT),
+ * optionally clearing it. Synchronises the device. */
+int fmlp_device_status(int reset);
+
+/* Static description of an error code. */
+const char* fmlp_error_string(int code);
+
+/* ABI version (major*100 + minor). */
+int fmlp_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHMLP_B200_H_ */
