@@ -12,15 +12,19 @@
 // the next products (flashmlp.py:212-235, :294-320).
 //
 // dW program (transposed so H^T and dZ^T land in TMEM as K-major A operands):
-//   Z^T  = W1c^T[smem] @ X_b^T[smem]     SS  M=128(e) N=128(b) K=D
-//   dH^T = W2c  [smem] @ dO_b^T[smem]    SS  M=128(e) N=128(b) K=D
+//   Z^T  = W1c^T[smem] @ X_b^T[smem]     SS  M=128(e) N=128(b) K=DP
+//   dH^T = W2c  [smem] @ dO_b^T[smem]    SS  M=128(e) N=128(b) K=DP
 //   dW2   += H^T [tmem] @ dO_b[smem]     TS  M=128(e) N=DP     K=128(b)
 //   dW1^T += dZ^T[tmem] @ X_b [smem]     TS  M=128(e) N=DP     K=128(b)
-// dX program:
-//   Z  = X_b [smem] @ W1c [smem]         SS  M=128(b) N=64(e)  K=D
-//   dH = dO_b[smem] @ W2c^T[smem]        SS  M=128(b) N=64(e)  K=D
+// The activation runs in two phases so the tensor pipe is not idle while it runs:
+// H^T = act(Z^T) as soon as Z^T is done (dW2 can start), then dZ^T once dH^T is done.
+// dX program (X_b and dO_b are copied once into TMEM, so every MMA reads only weights
+// from shared memory):
+//   Z  = X_b [tmem] @ W1c [smem]         TS  M=128(b) N=64(e)  K=DP
+//   dH = dO_b[tmem] @ W2c^T[smem]        TS  M=128(b) N=64(e)  K=DP
 //   dX += dZ[tmem] @ W1c^T[smem]         TS  M=128(b) N=DP     K=64(e)
 #include "fmlp_kernels.h"
+#include "fmlp_act.cuh"
 #include "fmlp_ptx.cuh"
 
 namespace fmlp {
@@ -57,58 +61,26 @@ struct BwdCfg {
   static constexpr int SMEM_USED = OFF_MISC + 16 + 1024;
   static constexpr int SMEM = SMEM_USED > 120 * 1024 ? SMEM_USED : 120 * 1024;
   static constexpr int TMEM_COLS = 512;
-  // TMEM columns
-  static constexpr int X_TM_DX = 0;        // dX accumulator, DP columns
-  static constexpr int X_TM_Z = DP;        // 2 buffers x (Z 64 | dH 64)
-  static constexpr int W_TM_DW1 = 0;       // dW1^T accumulator, DP columns
-  static constexpr int W_TM_DW2 = DP;      // dW2 accumulator, DP columns
-  static constexpr int W_TM_ZT = 2 * DP;   // Z^T 128 columns (H^T packed in place)
+  // TMEM columns, dX program
+  static constexpr int X_TM_X = 0;            // X_b packed, DP/2 columns
+  static constexpr int X_TM_DO = DP / 2;      // dO_b packed, DP/2 columns
+  static constexpr int X_TM_DX = DP;          // dX accumulator, DP columns
+  static constexpr int X_TM_Z = 2 * DP;       // 2 buffers x (Z 64 | dH 64)
+  // TMEM columns, dW program
+  static constexpr int W_TM_DW1 = 0;             // dW1^T accumulator, DP columns
+  static constexpr int W_TM_DW2 = DP;            // dW2 accumulator, DP columns
+  static constexpr int W_TM_ZT = 2 * DP;         // Z^T 128 columns (H^T packed in place)
   static constexpr int W_TM_DHT = 2 * DP + 128;  // dH^T 128 columns (dZ^T packed in place)
   static_assert(X_TM_Z + 2 * 128 <= TMEM_COLS, "TMEM budget (dX)");
   static_assert(W_TM_DHT + 128 <= TMEM_COLS, "TMEM budget (dW)");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static constexpr int NUM_THREADS = 320;
+  static constexpr int NUM_ACT_WARPS = 16;  // 4 per TMEM lane quadrant
+  static constexpr int FIRST_ACT_WARP = 3;  // warp 0 TMA, warps 1-2 MMA
+  static constexpr int NUM_THREADS = 32 * (FIRST_ACT_WARP + NUM_ACT_WARPS);
 };
 
-template <typename T, int ACT>
-__device__ __forceinline__ float act_h(float z) {
-  if constexpr (ACT == kLeakyRelu) {
-    return fmaxf(z, 0.01f * z);
-  } else if constexpr (ACT == kSilu) {
-    return z * sigmoid_fast(z);
-  } else if constexpr (ACT == kSigmoid) {
-    return sigmoid_fast(z);
-  } else {
-    return z;
-  }
-}
-
-// Given z and dh (fp32), returns h = act(z) and dz = dh * act'(z) (both unrounded fp32,
-// except that the derivative is formed from the rounded h where the reference does so).
-template <typename T, int ACT>
-__device__ __forceinline__ void act_bwd(float z, float dh, float& h, float& dz) {
-  if constexpr (ACT == kLeakyRelu) {
-    h = fmaxf(z, 0.01f * z);
-    dz = dh * (z >= 0.f ? 1.0f : 0.01f);  // flashmlp.py:33-34, :227-228
-  } else if constexpr (ACT == kSilu) {
-    const float s = sigmoid_fast(z);
-    h = z * s;
-    const float hr = Pack<T>::round(h);
-    dz = dh * (s + hr * (1.0f - s));  // d_silu(z, h) with rounded h, flashmlp.py:43-46
-  } else if constexpr (ACT == kSigmoid) {
-    h = sigmoid_fast(z);
-    const float hr = Pack<T>::round(h);
-    // dh * sig * (1 - sig) with sig the rounded h; (1 - sig) is formed in the input dtype
-    // as in flashmlp.py:232-233.
-    dz = (dh * hr) * Pack<T>::round(1.0f - hr);
-  } else {
-    h = z;
-    dz = dh;
-  }
-}
-
 template <int DP, typename T, int ACT>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(608, 1)
     fmlp_bwd_kernel(const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_w1,
@@ -117,7 +89,9 @@ __global__ void __launch_bounds__(320, 1)
                     T* __restrict__ dW1, T* __restrict__ dW2, int H, int B, int D, int E,
                     uint32_t* status) {
   using C = BwdCfg<DP>;
+  using St = ActState<T, ACT>;
   constexpr int BM = C::BM;
+  constexpr int NACT = C::NUM_ACT_WARPS;
   constexpr bool kBF = Pack<T>::kBF16;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -145,14 +119,16 @@ __global__ void __launch_bounds__(320, 1)
     idx = p % nB;  // B tile
   }
 
-  // Barrier assignment (both program kinds use the same slots differently).
-  uint64_t* in_full = bars + 0;        // dX: X_b+dO_b ; dW: W1c+W2c
-  uint64_t* ring_full = bars + 1;      // up to 4: dX: W stages ; dW: X/dO stages
-  uint64_t* ring_empty = bars + 5;     // up to 4
-  uint64_t* s_full = bars + 9;         // 2: products ready for the activation warps
-  uint64_t* hz_full = bars + 11;       // 2: packed operands written back to TMEM
-  uint64_t* acc_full = bars + 13;      // accumulators final
-  uint64_t* done_bar = bars + 14;      // all MMAs retired
+  // Barriers (both program kinds use the same slots differently).
+  uint64_t* in_full = bars + 0;     // dX: X_b+dO_b loaded ; dW: W1c+W2c loaded
+  uint64_t* ring_full = bars + 1;   // 4: dX: W stages ; dW: X/dO stages
+  uint64_t* ring_empty = bars + 5;  // 4
+  uint64_t* p_full = bars + 9;      // 2: dX: Z,dH of chunk ready ; dW: [0] Z^T, [1] dH^T ready
+  uint64_t* a_full = bars + 11;     // 2: dX: dZ packed ; dW: [0] H^T packed, [1] dZ^T packed
+  uint64_t* acc_full = bars + 13;   // accumulators final
+  uint64_t* xt_full = bars + 14;    // dX: X_b, dO_b copied into TMEM
+  uint64_t* done_bar = bars + 15;   // 2: all MMAs of MMA warp 1 / 2 retired
+  uint64_t* zfree = bars + 17;      // 2: dX: dZ of buffer read by its dX product
 
   if (threadIdx.x == 0) {
     misc[1] = 0;
@@ -160,14 +136,16 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(in_full, 1);
     for (int i = 0; i < 4; ++i) {
       mbar_init(&ring_full[i], 1);
-      mbar_init(&ring_empty[i], 1);
+      mbar_init(&ring_empty[i], 2);  // released by both MMA warps
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&hz_full[i], 8);
+      mbar_init(&p_full[i], 1);
+      mbar_init(&a_full[i], NACT);
+      mbar_init(&done_bar[i], 1);
+      mbar_init(&zfree[i], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(done_bar, 1);
+    mbar_init(acc_full, is_dw ? 2 : 1);  // dW: dW2 (warp 1) and dW1^T (warp 2)
+    mbar_init(xt_full, NACT);
     fence_mbar_init();
     tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_do);
@@ -182,6 +160,11 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  // Activation warps: warp (q, j) owns TMEM lanes [32q, 32q+32) and column slice j.
+  const int q = warp & 3;
+  const int j = (warp - C::FIRST_ACT_WARP) >> 2;
+  const uint32_t lane_off = uint32_t(q * 32) << 16;
 
   if (is_dw) {
     // ==================================================================== dW program
@@ -214,97 +197,125 @@ __global__ void __launch_bounds__(320, 1)
         for (uint32_t s = 0; s < XDS; ++s)
           if (nl > s) mbar_wait(&ring_full[s], ((nl - 1 - s) / XDS) & 1, drain);
       }
-    } else if (warp == 1) {
-      if (lane == 0) {
-        constexpr uint32_t idesc_s = make_idesc_f16(kBF, 128, 128, true, false);  // A MN, B K
-        constexpr uint32_t idesc_s2 = make_idesc_f16(kBF, 128, 128, false, false); // A K, B K
-        constexpr uint32_t idesc_w = make_idesc_f16(kBF, 128, DP, false, true);   // A tmem, B MN
-        const int nK = (D + 15) / 16;
-        const uint32_t w1a = smem_u32(sW1), w2a = smem_u32(sW2);
-        bool ok = mbar_wait(in_full, 0, ctx);
+    } else if (warp == 1 || warp == 2) {
+      // Two MMA warps, each owning one pair of products and its TMEM columns:
+      //   warp 1: dW2(i) += H^T(i) @ dO_i, then Z^T(i+1)   (columns of Z^T and dW2)
+      //   warp 2: dW1^T(i) += dZ^T(i) @ X_i, then dH^T(i+1) (columns of dH^T and dW1^T)
+      // so while the activation warps compute H^T(i+1) the tensor pipe runs dW1^T(i) and
+      // dH^T(i+1), and while they compute dZ^T(i) it runs dW2(i) and Z^T(i+1). Each warp's
+      // overwrite of a TMEM region follows its own read of it (same-thread MMA order).
+      const int m = warp - 1;
+      constexpr uint32_t idesc_s = make_idesc_f16(kBF, 128, 128, true, false);   // A MN, B K
+      constexpr uint32_t idesc_s2 = make_idesc_f16(kBF, 128, 128, false, false); // A K, B K
+      constexpr uint32_t idesc_w = make_idesc_f16(kBF, 128, DP, false, true);    // A tmem, B MN
+      // warp 1: A = W1c^T (MN-major), B = X tile (K-major), products into Z^T
+      // warp 2: A = W2c (K-major),    B = dO tile (K-major), products into dH^T
+      const uint64_t wdesc = m == 0 ? make_sdesc_sw128(smem_u32(sW1), DP * 128, 1024)
+                                    : make_sdesc_sw128(smem_u32(sW2), 16, 1024);
+      uint8_t* const sIn = m == 0 ? sX : sDO;    // tile read by this warp's first product
+      uint8_t* const sAcc = m == 0 ? sDO : sX;   // tile read by this warp's dW product
+      const uint32_t prod_col = m == 0 ? C::W_TM_ZT : C::W_TM_DHT;
+      const uint32_t acc_col = m == 0 ? C::W_TM_DW2 : C::W_TM_DW1;
+      auto issue_prod = [&](int bt) -> bool {  // Z^T(bt) or dH^T(bt)
+        const int s = bt % XDS;
+        if (!warp_wait(&ring_full[s], (bt / XDS) & 1, ctx)) return false;
         tc_fence_after();
-        for (int bt = 0; bt < nB && ok; ++bt) {
-          const int s = bt % XDS;
-          if (!(ok = mbar_wait(&ring_full[s], (bt / XDS) & 1, ctx))) break;
-          tc_fence_after();
-          const uint32_t xa = smem_u32(sX + s * C::TILE_BYTES);
-          const uint32_t da = smem_u32(sDO + s * C::TILE_BYTES);
-          // Z^T = W1c^T @ X_b^T ; dH^T = W2c @ dO_b^T
-          for (int k = 0; k < nK; ++k) {
-            const uint64_t a1 = make_sdesc_sw128(w1a + k * 2048, DP * 128, 1024);
-            const uint64_t bx = make_sdesc_sw128(xa + (k >> 2) * (BM * 128) + (k & 3) * 32, 16, 1024);
-            mma_ss(tmem + C::W_TM_ZT, a1, bx, idesc_s, k > 0 ? 1u : 0u);
+        if (elect_one()) {
+          const uint64_t bk = make_sdesc_sw128(smem_u32(sIn + s * C::TILE_BYTES), 16, 1024);
+#pragma unroll
+          for (int k = 0; k < DP / 16; ++k) {
+            const uint32_t aoff = m == 0 ? k * 2048 : (k >> 2) * (128 * 128) + (k & 3) * 32;
+            mma_ss(tmem + prod_col, sdesc_add(wdesc, aoff), sdesc_add(bk, (k >> 2) * (BM * 128) + (k & 3) * 32),
+                   m == 0 ? idesc_s : idesc_s2, k > 0 ? 1u : 0u);
           }
-          for (int k = 0; k < nK; ++k) {
-            const uint64_t a2 = make_sdesc_sw128(w2a + (k >> 2) * (128 * 128) + (k & 3) * 32, 16, 1024);
-            const uint64_t bd = make_sdesc_sw128(da + (k >> 2) * (BM * 128) + (k & 3) * 32, 16, 1024);
-            mma_ss(tmem + C::W_TM_DHT, a2, bd, idesc_s2, k > 0 ? 1u : 0u);
-          }
-          mma_commit(&s_full[0]);
-          if (!(ok = mbar_wait(&hz_full[0], bt & 1, ctx))) break;
-          tc_fence_after();
-          // dW2 += H^T @ dO_b ; dW1^T += dZ^T @ X_b   (K = 128 rows of the tile)
-          for (int k = 0; k < BM / 16; ++k) {
-            const int hf = k >> 2;
-            const uint32_t acol = hf * 64 + (k & 3) * 8;
-            const uint64_t bd = make_sdesc_sw128(da + k * 2048, BM * 128, 1024);
-            const uint64_t bx = make_sdesc_sw128(xa + k * 2048, BM * 128, 1024);
-            const uint32_t acc = (bt > 0 || k > 0) ? 1u : 0u;
-            mma_ts(tmem + C::W_TM_DW2, tmem + C::W_TM_ZT + acol, bd, idesc_w, acc);
-            mma_ts(tmem + C::W_TM_DW1, tmem + C::W_TM_DHT + acol, bx, idesc_w, acc);
-          }
-          mma_commit(&ring_empty[s]);
+          mma_commit(&p_full[m]);
         }
-        if (ok) mma_commit(acc_full);
-        mma_commit(done_bar);
-        mbar_wait(done_bar, 0, drain);
+        __syncwarp();
+        return true;
+      };
+      bool ok = warp_wait(in_full, 0, ctx);
+      tc_fence_after();
+      if (ok && nB > 0) ok = issue_prod(0);
+      for (int bt = 0; bt < nB && ok; ++bt) {
+        const int s = bt % XDS;
+        // dW2 += H^T @ dO_b (warp 1) / dW1^T += dZ^T @ X_b (warp 2), K = the 128 tile rows;
+        // the packed operand of B columns [16k, 16k+16) sits in slice k/2 at offset 8*(k%2).
+        if (!(ok = warp_wait(&a_full[m], bt & 1, ctx))) break;
+        tc_fence_after();
+        if (elect_one()) {
+          const uint64_t bm = make_sdesc_sw128(smem_u32(sAcc + s * C::TILE_BYTES), BM * 128, 1024);
+          const uint32_t acc0 = bt > 0 ? 1u : 0u;
+#pragma unroll
+          for (int k = 0; k < BM / 16; ++k)
+            mma_ts(tmem + acc_col, tmem + prod_col + (k >> 1) * 32 + (k & 1) * 8, sdesc_add(bm, k * 2048),
+                   idesc_w, k > 0 ? 1u : acc0);
+          mma_commit(&ring_empty[s]);  // this warp is done with stage s
+          if (bt + 1 == nB) mma_commit(acc_full);
+        }
+        __syncwarp();
+        if (bt + 1 < nB && !(ok = issue_prod(bt + 1))) break;
       }
+      if (elect_one()) mma_commit(&done_bar[m]);
+      __syncwarp();
+      warp_wait(&done_bar[m], 0, drain);
     } else {
-      const int q = warp & 3;
-      const int hf = (warp - 2) >> 2;
-      const uint32_t lane_off = uint32_t(q * 32) << 16;
+      // Activation warps: slice j = B columns [32j, 32j+32) of Z^T / dH^T.
+      const uint32_t zt = tmem + lane_off + C::W_TM_ZT + 32 * j;
+      const uint32_t dt = tmem + lane_off + C::W_TM_DHT + 32 * j;
       bool ok = true;
       for (int bt = 0; bt < nB && ok; ++bt) {
-        if (!(ok = mbar_wait(&s_full[0], bt & 1, ctx))) break;
+        St st[32];
+        // phase 1: H^T = act(Z^T), packed in place
+        if (!(ok = mbar_wait(&p_full[0], bt & 1, ctx))) break;
         tc_fence_after();
-        const uint32_t zt = tmem + lane_off + C::W_TM_ZT + 64 * hf;
-        const uint32_t dt = tmem + lane_off + C::W_TM_DHT + 64 * hf;
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          uint32_t vz[32], vd[32];
-          tmem_ld32_sync(zt + 32 * j, vz);
-          tmem_ld32_sync(dt + 32 * j, vd);
-          uint32_t ph[16], pd[16];
+        {
+          uint32_t v[32], ph[16];
+          tmem_ld32_sync(zt, v);
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            float h0, h1, d0, d1;
-            act_bwd<T, ACT>(__uint_as_float(vz[2 * i]), __uint_as_float(vd[2 * i]), h0, d0);
-            act_bwd<T, ACT>(__uint_as_float(vz[2 * i + 1]), __uint_as_float(vd[2 * i + 1]), h1, d1);
+            const float h0 = act_forward<T, ACT>(__uint_as_float(v[2 * i]), st[2 * i]);
+            const float h1 = act_forward<T, ACT>(__uint_as_float(v[2 * i + 1]), st[2 * i + 1]);
             ph[i] = Pack<T>::pack(h0, h1);
-            pd[i] = Pack<T>::pack(d0, d1);
           }
-          tmem_st16(zt + 16 * j, ph);
-          tmem_st16(dt + 16 * j, pd);
+          tmem_st16(zt, ph);
         }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&hz_full[0]);
+        if (lane == 0) mbar_arrive(&a_full[0]);
+        // phase 2: dZ^T = dH^T * act'(Z^T), packed in place (two halves of 16 columns)
+        if (!(ok = mbar_wait(&p_full[1], bt & 1, ctx))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          uint32_t v[16], pd[8];
+          tmem_ld16_sync(dt + 16 * u, v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            pd[i] = Pack<T>::pack(act_grad<T, ACT>(__uint_as_float(v[2 * i]), st[16 * u + 2 * i]),
+                                  act_grad<T, ACT>(__uint_as_float(v[2 * i + 1]), st[16 * u + 2 * i + 1]));
+          tmem_st8(dt + 8 * u, pd);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[1]);
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
         tc_fence_after();
         const int e = c * 128 + q * 32 + lane;
+        constexpr int OW = DP / 4;  // accumulator columns per warp
+        const int col0 = j * OW;
         // dW1^T rows are E, columns D: dW1[h, d, e]. Lanes hold consecutive e, so each
         // column d is one coalesced 64-byte store across the warp.
 #pragma unroll
-        for (int j = 0; j < (DP / 2) / 32; ++j) {
-          const int col0 = hf * (DP / 2) + 32 * j;
-          uint32_t v[32];
-          tmem_ld32_sync(tmem + lane_off + C::W_TM_DW1 + col0, v);
+        for (int u = 0; u < OW / 16; ++u) {
+          uint32_t v[16];
+          tmem_ld16_sync(tmem + lane_off + C::W_TM_DW1 + col0 + 16 * u, v);
           if (e < E) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int d = col0 + i;
+            for (int i = 0; i < 16; ++i) {
+              const int d = col0 + 16 * u + i;
               if (d < D) {
                 const uint32_t pk = Pack<T>::pack(__uint_as_float(v[i]), 0.f);
                 reinterpret_cast<uint16_t*>(dW1)[(size_t(h) * D + d) * E + e] = uint16_t(pk & 0xFFFFu);
@@ -314,19 +325,16 @@ __global__ void __launch_bounds__(320, 1)
         }
         T* w2row = dW2 + (size_t(h) * E + e) * D;
 #pragma unroll
-        for (int j = 0; j < (DP / 2) / 32; ++j) {
-          const int col0 = hf * (DP / 2) + 32 * j;
-          uint32_t v[32];
-          tmem_ld32_sync(tmem + lane_off + C::W_TM_DW2 + col0, v);
-          if (e < E && col0 < D) {
-            uint32_t p[16];
+        for (int u = 0; u < OW / 16; ++u) {
+          uint32_t v[16], p[8];
+          tmem_ld16_sync(tmem + lane_off + C::W_TM_DW2 + col0 + 16 * u, v);
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              p[i] = Pack<T>::pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-            uint4* dst = reinterpret_cast<uint4*>(w2row + col0);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              if (col0 + 8 * (i + 1) <= D) dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+          for (int i = 0; i < 8; ++i) p[i] = Pack<T>::pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+          const int cc = col0 + 16 * u;
+          if (e < E) {
+            uint4* dst = reinterpret_cast<uint4*>(w2row + cc);
+            if (cc + 8 <= D) dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+            if (cc + 16 <= D) dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
           }
         }
       }
@@ -362,100 +370,134 @@ __global__ void __launch_bounds__(320, 1)
           if (nl > s) mbar_wait(&ring_full[s], ((nl - 1 - s) / WSX) & 1, drain);
       }
     } else if (warp == 1) {
-      if (lane == 0) {
-        constexpr uint32_t idesc_z = make_idesc_f16(kBF, 128, 64, false, true);   // A K, B MN
-        constexpr uint32_t idesc_h = make_idesc_f16(kBF, 128, 64, false, false);  // A K, B K
-        constexpr uint32_t idesc_x = make_idesc_f16(kBF, 128, DP, false, false);  // A tmem, B K
-        const int nK = (D + 15) / 16;
-        const uint32_t xa = smem_u32(sX), da = smem_u32(sDO);
-        bool ok = mbar_wait(in_full, 0, ctx);
+      // MMA warp 1: Z(c) = X_b @ W1c and dH(c) = dO_b @ W2c^T into buffer c%2, running
+      // ahead of warp 2; before reusing a buffer it waits until warp 2's dX product has
+      // read the dZ packed there (zfree).
+      constexpr uint32_t idesc_z = make_idesc_f16(kBF, 128, 64, false, true);   // A tmem, B MN
+      constexpr uint32_t idesc_h = make_idesc_f16(kBF, 128, 64, false, false);  // A tmem, B K
+      bool ok = warp_wait(xt_full, 0, ctx);  // X_b, dO_b are in TMEM
+      tc_fence_after();
+      for (int c = 0; c < nEx && ok; ++c) {
+        const int s = c % WSX;
+        if (!(ok = warp_wait(&ring_full[s], (c / WSX) & 1, ctx))) break;
+        if (c >= 2 && !(ok = warp_wait(&zfree[c & 1], ((c >> 1) - 1) & 1, ctx))) break;
         tc_fence_after();
-        auto dx_step = [&](int cc) -> bool {
-          const uint32_t zb = cc & 1;
-          if (!mbar_wait(&hz_full[zb], (cc >> 1) & 1, ctx)) return false;
-          tc_fence_after();
-          const int s = cc % WSX;
-          const uint32_t wa = smem_u32(sW1 + s * C::W1X_BYTES);
-          const uint32_t zbase = tmem + C::X_TM_Z + zb * 128;
-          for (int k = 0; k < 4; ++k) {
-            const uint32_t acol = (k >> 1) * 32 + (k & 1) * 8;
-            const uint64_t bd = make_sdesc_sw128(wa + k * 32, 16, 1024);
-            mma_ts(tmem + C::X_TM_DX, zbase + acol, bd, idesc_x, (cc > 0 || k > 0) ? 1u : 0u);
-          }
-          mma_commit(&ring_empty[s]);
-          return true;
-        };
-        for (int c = 0; c < nEx && ok; ++c) {
-          const int s = c % WSX;
-          if (!(ok = mbar_wait(&ring_full[s], (c / WSX) & 1, ctx))) break;
-          tc_fence_after();
-          const uint32_t zb = c & 1;
-          const uint32_t zbase = tmem + C::X_TM_Z + zb * 128;
-          const uint32_t w1a = smem_u32(sW1 + s * C::W1X_BYTES);
-          const uint32_t w2a = smem_u32(sW2 + s * C::W2X_BYTES);
-          for (int k = 0; k < nK; ++k) {
-            const uint64_t ad = make_sdesc_sw128(xa + (k >> 2) * (BM * 128) + (k & 3) * 32, 16, 1024);
-            const uint64_t bd = make_sdesc_sw128(w1a + k * 2048, DP * 128, 1024);
-            mma_ss(zbase, ad, bd, idesc_z, k > 0 ? 1u : 0u);
-          }
-          for (int k = 0; k < nK; ++k) {
-            const uint64_t ad = make_sdesc_sw128(da + (k >> 2) * (BM * 128) + (k & 3) * 32, 16, 1024);
-            const uint64_t bd = make_sdesc_sw128(w2a + (k >> 2) * (64 * 128) + (k & 3) * 32, 16, 1024);
-            mma_ss(zbase + 64, ad, bd, idesc_h, k > 0 ? 1u : 0u);
-          }
-          mma_commit(&s_full[zb]);
-          if (c > 0) ok = dx_step(c - 1);
+        if (elect_one()) {
+          const uint32_t zbase = tmem + C::X_TM_Z + (c & 1) * 128;
+          const uint64_t w1m = make_sdesc_sw128(smem_u32(sW1 + s * C::W1X_BYTES), DP * 128, 1024);
+          const uint64_t w2k = make_sdesc_sw128(smem_u32(sW2 + s * C::W2X_BYTES), 16, 1024);
+#pragma unroll
+          for (int k = 0; k < DP / 16; ++k)
+            mma_ts(zbase, tmem + C::X_TM_X + 8 * k, sdesc_add(w1m, k * 2048), idesc_z, k > 0 ? 1u : 0u);
+#pragma unroll
+          for (int k = 0; k < DP / 16; ++k)
+            mma_ts(zbase + 64, tmem + C::X_TM_DO + 8 * k,
+                   sdesc_add(w2k, (k >> 2) * (64 * 128) + (k & 3) * 32), idesc_h, k > 0 ? 1u : 0u);
+          mma_commit(&p_full[c & 1]);
+          mma_commit(&ring_empty[s]);  // warp 1 is done with stage s
         }
-        if (ok && nEx > 0) ok = dx_step(nEx - 1);
-        if (ok) mma_commit(acc_full);
-        mma_commit(done_bar);
-        mbar_wait(done_bar, 0, drain);
+        __syncwarp();
       }
-    } else {
-      const int q = warp & 3;
-      const int hf = (warp - 2) >> 2;
-      const uint32_t lane_off = uint32_t(q * 32) << 16;
+      if (elect_one()) mma_commit(&done_bar[0]);
+      __syncwarp();
+      warp_wait(&done_bar[0], 0, drain);
+    } else if (warp == 2) {
+      // MMA warp 2: dX += dZ(c) @ W1c^T once the activation warps have packed dZ(c).
+      constexpr uint32_t idesc_x = make_idesc_f16(kBF, 128, DP, false, false);  // A tmem, B K
       bool ok = true;
       for (int c = 0; c < nEx && ok; ++c) {
         const uint32_t zb = c & 1;
-        if (!(ok = mbar_wait(&s_full[zb], (c >> 1) & 1, ctx))) break;
+        if (!(ok = warp_wait(&a_full[zb], (c >> 1) & 1, ctx))) break;
         tc_fence_after();
-        const uint32_t za = tmem + lane_off + C::X_TM_Z + zb * 128 + 32 * hf;
-        uint32_t vz[32], vd[32];
-        tmem_ld32_sync(za, vz);
-        tmem_ld32_sync(za + 64, vd);
-        uint32_t pd[16];
+        if (elect_one()) {
+          const int s = c % WSX;
+          const uint64_t wk = make_sdesc_sw128(smem_u32(sW1 + s * C::W1X_BYTES), 16, 1024);
+          const uint32_t zbase = tmem + C::X_TM_Z + zb * 128;
+          const uint32_t acc0 = c > 0 ? 1u : 0u;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float h0, h1, d0, d1;
-          act_bwd<T, ACT>(__uint_as_float(vz[2 * i]), __uint_as_float(vd[2 * i]), h0, d0);
-          act_bwd<T, ACT>(__uint_as_float(vz[2 * i + 1]), __uint_as_float(vd[2 * i + 1]), h1, d1);
-          pd[i] = Pack<T>::pack(d0, d1);
+          for (int k = 0; k < 4; ++k)  // dZ of E columns [16k, 16k+16) is in slice k
+            mma_ts(tmem + C::X_TM_DX, zbase + 16 * k, sdesc_add(wk, k * 32), idesc_x, k > 0 ? 1u : acc0);
+          mma_commit(&zfree[zb]);
+          mma_commit(&ring_empty[s]);  // warp 2 is done with stage s
+          if (c + 1 == nEx) mma_commit(acc_full);
         }
-        tmem_st16(za, pd);
+        __syncwarp();
+      }
+      if (elect_one()) mma_commit(&done_bar[1]);
+      __syncwarp();
+      warp_wait(&done_bar[1], 0, drain);
+    } else {
+      bool ok = mbar_wait(in_full, 0, ctx);
+      // Copy this warp's share of X_b and dO_b from the swizzled smem tiles into TMEM as
+      // packed K-major A operands (column w holds elements 2w, 2w+1 of the row).
+      if (ok) {
+        const int r = q * 32 + lane;  // tile row == TMEM lane
+        constexpr int WPW = DP / 8;   // 32-bit words per warp slice (DP/2 words per row)
+        const int e0 = j * WPW * 2;   // first element of the slice
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const uint8_t* tile = t == 0 ? sX : sDO;
+          uint32_t w[WPW];
+#pragma unroll
+          for (int g = 0; g < WPW / 4; ++g) {  // 16-byte chunks of 8 elements
+            const int el = e0 + 8 * g;
+            const int region = el >> 6, chunk = (el & 63) >> 3;
+            const uint4 v = *reinterpret_cast<const uint4*>(tile + region * (BM * 128) + r * 128 +
+                                                            ((chunk ^ (r & 7)) << 4));
+            w[4 * g] = v.x, w[4 * g + 1] = v.y, w[4 * g + 2] = v.z, w[4 * g + 3] = v.w;
+          }
+          const uint32_t dst = tmem + lane_off + (t == 0 ? C::X_TM_X : C::X_TM_DO) + j * WPW;
+          if constexpr (WPW == 16) {
+            tmem_st16(dst, w);
+          } else {
+            tmem_st8(dst, w);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xt_full);
+      // Per E chunk: slice j = E columns [16j, 16j+16) of Z and dH.
+      for (int c = 0; c < nEx && ok; ++c) {
+        const uint32_t zb = c & 1;
+        if (!(ok = mbar_wait(&p_full[zb], (c >> 1) & 1, ctx))) break;
+        tc_fence_after();
+        const uint32_t za = tmem + lane_off + C::X_TM_Z + zb * 128 + 16 * j;
+        uint32_t vz[16], vd[16], pd[8];
+        tmem_ld16_sync(za, vz);
+        tmem_ld16_sync(za + 64, vd);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          St s0, s1;
+          act_forward<T, ACT>(__uint_as_float(vz[2 * i]), s0);
+          act_forward<T, ACT>(__uint_as_float(vz[2 * i + 1]), s1);
+          pd[i] = Pack<T>::pack(act_grad<T, ACT>(__uint_as_float(vd[2 * i]), s0),
+                                act_grad<T, ACT>(__uint_as_float(vd[2 * i + 1]), s1));
+        }
+        tmem_st8(za, pd);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&hz_full[zb]);
+        if (lane == 0) mbar_arrive(&a_full[zb]);
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
         tc_fence_after();
         const int row = bt * BM + q * 32 + lane;
         T* xrow = dX + (size_t(h) * B + row) * D;
+        constexpr int OW = DP / 4;
+        const int col0 = j * OW;
 #pragma unroll
-        for (int j = 0; j < (DP / 2) / 32; ++j) {
-          const int col0 = hf * (DP / 2) + 32 * j;
-          uint32_t v[32];
-          tmem_ld32_sync(tmem + lane_off + C::X_TM_DX + col0, v);
-          if (row < B && col0 < D) {
-            uint32_t p[16];
+        for (int u = 0; u < OW / 16; ++u) {
+          uint32_t v[16], p[8];
+          tmem_ld16_sync(tmem + lane_off + C::X_TM_DX + col0 + 16 * u, v);
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              p[i] = Pack<T>::pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-            uint4* dst = reinterpret_cast<uint4*>(xrow + col0);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              if (col0 + 8 * (i + 1) <= D) dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+          for (int i = 0; i < 8; ++i) p[i] = Pack<T>::pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+          const int cc = col0 + 16 * u;
+          if (row < B) {
+            uint4* dst = reinterpret_cast<uint4*>(xrow + cc);
+            if (cc + 8 <= D) dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+            if (cc + 16 <= D) dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
           }
         }
       }

@@ -151,6 +151,7 @@ int fmlp_fwd(const void* x, const void* w1, const void* w2, void* o, int H, int 
   a.act = act;
   const long long tiles = (long long)H * ((B + kRows - 1) / kRows);
   a.grid = int(tiles < dev->sm_count ? tiles : dev->sm_count);
+  a.sm_count = dev->sm_count;
   a.status = dev->status;
   a.stream = st;
   return cuda_rc(launch_fwd(a));

@@ -8,13 +8,14 @@
 // Design (one CTA per SM, persistent over (head, 128-row tile) work items):
 //   warp 0      TMA producer: X tile (double-buffered), W1/W2 E-chunks (2-stage rings)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..9  activation + epilogue: Z (fp32, TMEM) -> act -> H (16-bit, written back
-//               into the same TMEM columns) ; O (TMEM) -> global
+//   warps 2..17 activation + epilogue (4 per TMEM lane quadrant): Z (fp32, TMEM) -> act
+//               -> H (16-bit, written back into the same TMEM columns) ; O (TMEM) -> global
 // GEMM1  Z[zb]  = X[smem]  @ W1c[smem]     (SS, M=128, N=ET,  K=D)
 // GEMM2  O[ob] += H[tmem]  @ W2c[smem]     (TS, M=128, N=DP,  K=ET)
 // Z is double-buffered so GEMM1 of chunk c+1 runs while chunk c is activated; O is
 // double-buffered (DP<=128) so the epilogue of one tile overlaps the next tile.
 #include "fmlp_kernels.h"
+#include "fmlp_act.cuh"
 #include "fmlp_ptx.cuh"
 
 namespace fmlp {
@@ -46,24 +47,14 @@ struct FwdCfg {
   static constexpr int TMEM_COLS = 512;
   static_assert(TMEM_Z + 2 * ET <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static constexpr int NUM_THREADS = 320;
+  static constexpr int NUM_ACT_WARPS = 16;  // 4 per TMEM lane quadrant
+  static constexpr int NUM_THREADS = 32 * (2 + NUM_ACT_WARPS);
+  static constexpr int SW = ET / 4;  // Z columns per activation warp
+  static constexpr int OW = DP / 4;  // O columns per activation warp
 };
 
-template <typename T, int ACT>
-__device__ __forceinline__ float act_fwd(float z) {
-  if constexpr (ACT == kLeakyRelu) {
-    return fmaxf(z, 0.01f * z);  // == where(z >= 0, z, 0.01 z) for slope < 1
-  } else if constexpr (ACT == kSilu) {
-    return z * sigmoid_fast(z);
-  } else if constexpr (ACT == kSigmoid) {
-    return sigmoid_fast(z);
-  } else {
-    return z;
-  }
-}
-
 template <int DP, typename T, int ACT>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(576, 1)
     fmlp_fwd_kernel(const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_w1,
                     const __grid_constant__ CUtensorMap tm_w2, T* __restrict__ O, int H, int B,
@@ -116,11 +107,11 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&z_full[i], 1);
-      mbar_init(&h_full[i], 8);
+      mbar_init(&h_full[i], C::NUM_ACT_WARPS);
     }
     for (int i = 0; i < NO; ++i) {
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 8);
+      mbar_init(&o_empty[i], C::NUM_ACT_WARPS);
     }
     mbar_init(done_bar, 1);
     fence_mbar_init();
@@ -189,88 +180,98 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr bool kBF = Pack<T>::kBF16;
-      constexpr uint32_t idesc1 = make_idesc_f16(kBF, BM, ET, false, true);
-      constexpr uint32_t idesc2 = make_idesc_f16(kBF, BM, DP, false, true);
-      const int nK1 = (D + 15) / 16;
-      uint32_t c1 = 0, c2 = 0, zc = 0, it = 0;
-      bool ok = true;
-      const uint32_t sX_a = smem_u32(sX), sW1_a = smem_u32(sW1), sW2_a = smem_u32(sW2);
+    // The whole warp runs the schedule (warp-uniform waits); one elected lane issues
+    // each unrolled burst of MMAs and the commits that follow it.
+    constexpr bool kBF = Pack<T>::kBF16;
+    constexpr uint32_t idesc1 = make_idesc_f16(kBF, BM, ET, false, true);
+    constexpr uint32_t idesc2 = make_idesc_f16(kBF, BM, DP, false, true);
+    uint32_t c1 = 0, c2 = 0, zc = 0, it = 0;
+    bool ok = true;
+    const uint32_t sX_a = smem_u32(sX), sW1_a = smem_u32(sW1), sW2_a = smem_u32(sW2);
 
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
-        const int xb = it % XB;
-        const uint32_t xn = it / XB;
-        const int ob = it % NO;
-        const uint32_t on = it / NO;
-        if (!(ok = mbar_wait(&x_full[xb], xn & 1, ctx))) break;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+      const int xb = it % XB;
+      const uint32_t xn = it / XB;
+      const int ob = it % NO;
+      const uint32_t on = it / NO;
+      if (!(ok = warp_wait(&x_full[xb], xn & 1, ctx))) break;
+      tc_fence_after();
+      const uint64_t xdesc = make_sdesc_sw128(sX_a + xb * C::X_BYTES, 16, 1024);
+
+      // GEMM1 of one E chunk into Z buffer (zidx & 1). K runs over the padded DP: the
+      // columns of X and rows of W1 beyond D are zero-filled by TMA.
+      auto gemm1 = [&](uint32_t zidx) -> bool {
+        const int s = c1 % WS;
+        const uint32_t n = c1 / WS;
+        ++c1;
+        if (!warp_wait(&w1_full[s], n & 1, ctx)) return false;
         tc_fence_after();
-        const uint32_t xa = sX_a + xb * C::X_BYTES;
-
-        // GEMM1 for local chunk index `c` into Z buffer (zc_at % 2).
-        auto gemm1 = [&](uint32_t zidx) -> bool {
-          const int s = c1 % WS;
-          const uint32_t n = c1 / WS;
-          ++c1;
-          if (!mbar_wait(&w1_full[s], n & 1, ctx)) return false;
-          tc_fence_after();
-          const uint32_t zb = zidx & 1;
+        const uint32_t zb = zidx & 1;
+        if (elect_one()) {
           const uint32_t d_tmem = tmem + C::TMEM_Z + zb * ET;
-          const uint32_t wa = sW1_a + s * C::W1_BYTES;
-          for (int k = 0; k < nK1; ++k) {
-            const uint64_t ad = make_sdesc_sw128(xa + (k >> 2) * (BM * 128) + (k & 3) * 32, 16, 1024);
-            const uint64_t bd = make_sdesc_sw128(wa + k * 2048, DP * 128, 1024);
-            mma_ss(d_tmem, ad, bd, idesc1, k > 0 ? 1u : 0u);
-          }
+          const uint64_t wdesc = make_sdesc_sw128(sW1_a + s * C::W1_BYTES, DP * 128, 1024);
+#pragma unroll
+          for (int k = 0; k < DP / 16; ++k)
+            mma_ss(d_tmem, sdesc_add(xdesc, (k >> 2) * (BM * 128) + (k & 3) * 32),
+                   sdesc_add(wdesc, k * 2048), idesc1, k > 0 ? 1u : 0u);
           mma_commit(&z_full[zb]);
           mma_commit(&w1_empty[s]);
-          return true;
-        };
+        }
+        __syncwarp();
+        return true;
+      };
 
-        if (!(ok = gemm1(zc))) break;
-        for (int c = 0; c < nE; ++c) {
-          const uint32_t zcur = zc + c;
-          if (c + 1 < nE) {
-            if (!(ok = gemm1(zcur + 1))) break;
-          }
-          if (c + 1 == nE) mma_commit(&x_empty[xb]);  // last reader of this X buffer issued
-          if (c == 0) {
-            if (!(ok = mbar_wait(&o_empty[ob], (on & 1) ^ 1, ctx))) break;
-          }
-          const uint32_t zb = zcur & 1;
-          if (!(ok = mbar_wait(&h_full[zb], (zcur >> 1) & 1, ctx))) break;
-          const int s = c2 % WS;
-          const uint32_t n = c2 / WS;
-          ++c2;
-          if (!(ok = mbar_wait(&w2_full[s], n & 1, ctx))) break;
-          tc_fence_after();
-          const uint32_t wa = sW2_a + s * C::W2_BYTES;
+      if (!(ok = gemm1(zc))) break;
+      for (int c = 0; c < nE; ++c) {
+        const uint32_t zcur = zc + c;
+        if (c + 1 < nE) {
+          if (!(ok = gemm1(zcur + 1))) break;
+        } else {
+          if (elect_one()) mma_commit(&x_empty[xb]);  // every reader of this X buffer issued
+          __syncwarp();
+        }
+        if (c == 0) {
+          if (!(ok = warp_wait(&o_empty[ob], (on & 1) ^ 1, ctx))) break;
+        }
+        const uint32_t zb = zcur & 1;
+        if (!(ok = warp_wait(&h_full[zb], (zcur >> 1) & 1, ctx))) break;
+        const int s = c2 % WS;
+        const uint32_t n = c2 / WS;
+        ++c2;
+        if (!(ok = warp_wait(&w2_full[s], n & 1, ctx))) break;
+        tc_fence_after();
+        if (elect_one()) {
+          const uint64_t wdesc = make_sdesc_sw128(sW2_a + s * C::W2_BYTES, ET * 128, 1024);
           const uint32_t o_tmem = tmem + C::TMEM_O + ob * DP;
           const uint32_t h_base = tmem + C::TMEM_Z + zb * ET;
+          const uint32_t acc0 = c > 0 ? 1u : 0u;
+#pragma unroll
           for (int k = 0; k < ET / 16; ++k) {
-            // H of E columns [16k, 16k+16) was packed by the activation warp that owns that
-            // column half, at the start of its half: see the activation loop below.
-            const int e0 = 16 * k;
-            const int hf = e0 / (ET / 2);
-            const int within = e0 - hf * (ET / 2);
-            const uint32_t a_tmem = h_base + hf * (ET / 2) + within / 2;
-            const uint64_t bd = make_sdesc_sw128(wa + k * 2048, ET * 128, 1024);
-            mma_ts(o_tmem, a_tmem, bd, idesc2, (c > 0 || k > 0) ? 1u : 0u);
+            // H of E columns [16k, 16k+16) was packed by the activation warp that owns
+            // that column slice, at the start of its slice (see the activation loop below).
+            const int sl = (16 * k) / C::SW;
+            const int within = 16 * k - sl * C::SW;
+            mma_ts(o_tmem, h_base + sl * C::SW + within / 2, sdesc_add(wdesc, k * 2048), idesc2,
+                   k > 0 ? 1u : acc0);
           }
           mma_commit(&w2_empty[s]);
+          if (c + 1 == nE) mma_commit(&o_full[ob]);
         }
-        if (!ok) break;
-        zc += nE;
-        mma_commit(&o_full[ob]);
+        __syncwarp();
       }
-      // Drain every MMA issued by this thread before TMEM is released.
-      mma_commit(done_bar);
-      mbar_wait(done_bar, 0, WaitCtx{misc + 2, status});
+      zc += nE;
     }
+    // Drain every MMA issued by this warp before TMEM is released.
+    if (elect_one()) mma_commit(done_bar);
+    __syncwarp();
+    warp_wait(done_bar, 0, WaitCtx{misc + 2, status});
   } else {
     // ------------------------------------------------------------------ activation + epilogue
-    const int q = warp & 3;            // TMEM lane quadrant this warp may access
-    const int hf = (warp - 2) >> 2;    // column half handled by this warp
+    // 16 warps: warp (q, j) owns TMEM lanes [32q, 32q+32) (its hardware quadrant) and
+    // column slice j of every Z chunk and of the O tile.
+    const int q = warp & 3;
+    const int j = (warp - 2) >> 2;
+    constexpr int SW = C::SW, OW = C::OW;
     const uint32_t lane_off = uint32_t(q * 32) << 16;
     uint32_t zc = 0, it = 0;
     bool ok = true;
@@ -282,21 +283,25 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t zb = zc & 1;
         if (!(ok = mbar_wait(&z_full[zb], (zc >> 1) & 1, ctx))) break;
         tc_fence_after();
-        const uint32_t zaddr = tmem + lane_off + C::TMEM_Z + zb * ET + hf * (ET / 2);
+        const uint32_t zaddr = tmem + lane_off + C::TMEM_Z + zb * ET + j * SW;
+        // H for these SW columns is packed two per column into the first SW/2 columns of
+        // the slice, which this warp has just read.
+        if constexpr (SW == 32) {
+          uint32_t v[32], p[16];
+          tmem_ld32_sync(zaddr, v);
 #pragma unroll
-        for (int j = 0; j < (ET / 2) / 32; ++j) {
-          uint32_t v[32];
-          tmem_ld32_sync(zaddr + 32 * j, v);
-          uint32_t p[16];
+          for (int i = 0; i < 16; ++i)
+            p[i] = Pack<T>::pack(act_fwd<T, ACT>(__uint_as_float(v[2 * i])),
+                                 act_fwd<T, ACT>(__uint_as_float(v[2 * i + 1])));
+          tmem_st16(zaddr, p);
+        } else {
+          uint32_t v[16], p[8];
+          tmem_ld16_sync(zaddr, v);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float a0 = act_fwd<T, ACT>(__uint_as_float(v[2 * i]));
-            const float a1 = act_fwd<T, ACT>(__uint_as_float(v[2 * i + 1]));
-            p[i] = Pack<T>::pack(a0, a1);
-          }
-          // Packed H for these 32 columns goes to 16 columns at the start of the half; the
-          // Z columns it overwrites were consumed by this warp in this or an earlier step.
-          tmem_st16(zaddr + 16 * j, p);
+          for (int i = 0; i < 8; ++i)
+            p[i] = Pack<T>::pack(act_fwd<T, ACT>(__uint_as_float(v[2 * i])),
+                                 act_fwd<T, ACT>(__uint_as_float(v[2 * i + 1])));
+          tmem_st8(zaddr, p);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -304,25 +309,32 @@ __global__ void __launch_bounds__(320, 1)
         if (lane == 0) mbar_arrive(&h_full[zb]);
       }
       if (!ok) break;
-      // Epilogue: O (fp32, TMEM) -> input dtype -> global.
+      // Epilogue: O (fp32, TMEM) -> input dtype -> global, 16-byte stores per row.
       if (!(ok = mbar_wait(&o_full[ob], on & 1, ctx))) break;
       tc_fence_after();
       const int row = bt * BM + q * 32 + lane;
       T* orow = O + (size_t(h) * B + row) * D;
-      const uint32_t oaddr = tmem + lane_off + C::TMEM_O + ob * DP;
+      const uint32_t oaddr = tmem + lane_off + C::TMEM_O + ob * DP + j * OW;
 #pragma unroll
-      for (int j = 0; j < (DP / 2) / 32; ++j) {
-        const int col0 = hf * (DP / 2) + 32 * j;
-        uint32_t v[32];
-        tmem_ld32_sync(oaddr + col0, v);
-        if (row < B && col0 < D) {
-          uint32_t p[16];
+      for (int u = 0; u < (OW + 31) / 32; ++u) {
+        constexpr int NC = OW < 32 ? OW : 32;
+        const int col0 = j * OW + u * NC;
+        uint32_t p[NC / 2];
+        if constexpr (NC == 32) {
+          uint32_t v[32];
+          tmem_ld32_sync(oaddr + u * 32, v);
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            p[i] = Pack<T>::pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+          for (int i = 0; i < 16; ++i) p[i] = Pack<T>::pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+        } else {
+          uint32_t v[16];
+          tmem_ld16_sync(oaddr, v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) p[i] = Pack<T>::pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+        }
+        if (row < B) {
           uint4* dst = reinterpret_cast<uint4*>(orow + col0);
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+          for (int i = 0; i < NC / 8; ++i)
             if (col0 + 8 * (i + 1) <= D) dst[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
         }
       }
@@ -376,8 +388,8 @@ int fwd_smem_bytes(int dp) {
 
 cudaError_t launch_fwd(const FwdLaunch& a) {
   switch (a.dp) {
-    case 64: return launch_fwd_dt<64>(a);
-    case 128: return launch_fwd_dt<128>(a);
+    case 64:
+    case 128: return launch_fwd_pair(a);
     case 256: return launch_fwd_dt<256>(a);
   }
   return cudaErrorInvalidValue;

@@ -15,7 +15,8 @@ struct FwdLaunch {
   int dp;             // D rounded up to a multiple of 64 (64, 128 or 256)
   int bf16;           // 1 = bfloat16, 0 = float16
   int act;            // fmlp::Act
-  int grid;           // persistent CTAs
+  int grid;           // persistent CTAs (single-tile kernel)
+  int sm_count;       // SMs of the device
   uint32_t* status;   // device status word
   cudaStream_t stream;
 };
@@ -44,7 +45,8 @@ constexpr int kBwdEtW = 128;  // E chunk owned by one dW program
 
 int fwd_smem_bytes(int dp);
 int bwd_smem_bytes(int dp);
-cudaError_t launch_fwd(const FwdLaunch& a);
+cudaError_t launch_fwd(const FwdLaunch& a);       // picks the kernel for a.dp
+cudaError_t launch_fwd_pair(const FwdLaunch& a);  // two row tiles per CTA, D <= 128
 cudaError_t launch_bwd(const BwdLaunch& a);
 
 }  // namespace fmlp
