@@ -65,6 +65,43 @@ __device__ __forceinline__ float act_grad(float dh, const ActState<T, ACT>& st) 
   }
 }
 
+// Activates a pair: returns H rounded and packed (z0 in the low half) and records the
+// derivative state; the rounded H is read back from the packed word with integer ops.
+template <typename T, int ACT>
+__device__ __forceinline__ uint32_t act_pair(float z0, float z1, ActState<T, ACT>& s0, ActState<T, ACT>& s1) {
+  float h0, h1;
+  if constexpr (ACT == kLeakyRelu) {
+    s0.pos = z0 >= 0.f;
+    s1.pos = z1 >= 0.f;
+    h0 = fmaxf(z0, 0.01f * z0);
+    h1 = fmaxf(z1, 0.01f * z1);
+  } else if constexpr (ACT == kSilu) {
+    s0.s = sigmoid_fast(z0);
+    s1.s = sigmoid_fast(z1);
+    h0 = z0 * s0.s;
+    h1 = z1 * s1.s;
+  } else if constexpr (ACT == kSigmoid) {
+    h0 = sigmoid_fast(z0);
+    h1 = sigmoid_fast(z1);
+  } else {
+    h0 = z0;
+    h1 = z1;
+  }
+  const uint32_t p = Pack<T>::pack(h0, h1);
+  if constexpr (ACT == kSilu || ACT == kSigmoid) {
+    s0.hr = Pack<T>::lo(p);
+    s1.hr = Pack<T>::hi(p);
+  }
+  return p;
+}
+
+// dz = dh * act'(z) for a pair, rounded and packed.
+template <typename T, int ACT>
+__device__ __forceinline__ uint32_t grad_pair(float dh0, float dh1, const ActState<T, ACT>& s0,
+                                              const ActState<T, ACT>& s1) {
+  return Pack<T>::pack(act_grad<T, ACT>(dh0, s0), act_grad<T, ACT>(dh1, s1));
+}
+
 // Packs 2*N fp32 values (activated) into N 16-bit pairs.
 template <typename T, int ACT, int N>
 __device__ __forceinline__ void act_pack(const uint32_t* v, uint32_t* p) {

@@ -189,8 +189,7 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
   if ((rc = encode3d(&a.tm_x, x, bf, D, B, H, 64, kRows))) return rc;
   if ((rc = encode3d(&a.tm_do, dO, bf, D, B, H, 64, kRows))) return rc;
   if ((rc = encode3d(&a.tm_w1, w1, bf, E, D, H, 64, a.dp))) return rc;
-  if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, kBwdEtX))) return rc;
-  if ((rc = encode3d(&a.tm_w2w, w2, bf, D, E, H, 64, kBwdEtW))) return rc;
+  if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, kBwdEt))) return rc;
   a.dx = dx, a.dw1 = dw1, a.dw2 = dw2;
   a.H = H, a.B = B, a.D = D, a.E = E;
   a.bf16 = bf;

@@ -25,8 +25,7 @@ struct BwdLaunch {
   CUtensorMap tm_x;    // X  {D, B, H}, box {64, 128, 1}
   CUtensorMap tm_do;   // dO {D, B, H}, box {64, 128, 1}
   CUtensorMap tm_w1;   // W1 {E, D, H}, box {64, DP, 1}
-  CUtensorMap tm_w2;   // W2 {D, E, H}, box {64, 64, 1}   (64-row E chunks)
-  CUtensorMap tm_w2w;  // W2 {D, E, H}, box {64, 128, 1}  (128-row E chunks, dW programs)
+  CUtensorMap tm_w2;   // W2 {D, E, H}, box {64, 128, 1}  (128-row E chunks)
   void* dx;
   void* dw1;
   void* dw2;
@@ -40,8 +39,7 @@ struct BwdLaunch {
 constexpr int kRows = 128;  // rows of a B tile (tcgen05 M)
 
 inline int fwd_et(int dp) { return dp <= 128 ? 128 : 64; }
-constexpr int kBwdEtX = 64;   // E chunk of the dX programs
-constexpr int kBwdEtW = 128;  // E chunk owned by one dW program
+constexpr int kBwdEt = 128;  // E chunk of both backward program kinds
 
 int fwd_smem_bytes(int dp);
 int bwd_smem_bytes(int dp);

@@ -238,6 +238,29 @@ __device__ __forceinline__ void tmem_ld32x2_sync(uint32_t taddr0, uint32_t taddr
       : "memory");
 }
 
+// Asynchronous 16-column load: the registers are valid only after tmem_wait_ld_dep(r).
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Waits for every outstanding tcgen05.ld of this thread. The registers of the last
+// asynchronous load are in/out operands, so no use of them can move above the wait.
+__device__ __forceinline__ void tmem_wait_ld_dep(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
+                 "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
 // Warp-wide: 8 registers per thread -> 32 lanes x 8 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile(
@@ -317,6 +340,9 @@ struct Pack<__nv_bfloat16> {
   __device__ __forceinline__ static float round(float x) {
     return __bfloat162float(__float2bfloat16_rn(x));
   }
+  // The two values of a packed pair, widened back to fp32 (exact; integer ops only).
+  __device__ __forceinline__ static float lo(uint32_t p) { return __uint_as_float(p << 16); }
+  __device__ __forceinline__ static float hi(uint32_t p) { return __uint_as_float(p & 0xFFFF0000u); }
 };
 template <>
 struct Pack<__half> {
@@ -326,6 +352,12 @@ struct Pack<__half> {
     return *reinterpret_cast<uint32_t*>(&v);
   }
   __device__ __forceinline__ static float round(float x) { return __half2float(__float2half_rn(x)); }
+  __device__ __forceinline__ static float lo(uint32_t p) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(p & 0xFFFFu)));
+  }
+  __device__ __forceinline__ static float hi(uint32_t p) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(p >> 16)));
+  }
 };
 
 // tanh on the SFU (one MUFU op), max relative error about 2^-11.
