@@ -583,6 +583,7 @@ int bwd_smem_bytes(int dp) {
   switch (dp) {
     case 64: return BwdCfg<64>::SMEM;
     case 128: return BwdCfg<128>::SMEM;
+    case 256: return bwd256_smem_bytes();
   }
   return -1;
 }
@@ -591,6 +592,7 @@ cudaError_t launch_bwd(const BwdLaunch& a) {
   switch (a.dp) {
     case 64: return launch_bwd_dt<64>(a);
     case 128: return launch_bwd_dt<128>(a);
+    case 256: return launch_bwd256(a);
   }
   return cudaErrorNotSupported;
 }

@@ -114,7 +114,7 @@ const char* fmlp_error_string(int code) {
     case FMLP_ERR_INVALID_SHAPE: return "invalid shape (negative size or too large)";
     case FMLP_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype (only float16 and bfloat16)";
     case FMLP_ERR_UNSUPPORTED_D:
-      return "unsupported hidden dim D (needs D % 16 == 0, D <= 256 forward, D <= 128 backward)";
+      return "unsupported hidden dim D (needs D % 16 == 0 and D <= 256)";
     case FMLP_ERR_UNSUPPORTED_E: return "unsupported intermediate dim E (needs E % 8 == 0)";
     case FMLP_ERR_MISALIGNED: return "tensor data pointer is not 16-byte aligned";
     case FMLP_ERR_CUDA: return "CUDA runtime error";
@@ -168,7 +168,7 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
   (void)workspace;
   int rc = check_common(H, B, D, E, dtype);
   if (rc) return rc;
-  if (D % 16 != 0 || D > 128) return FMLP_ERR_UNSUPPORTED_D;
+  if (D % 16 != 0 || D > 256) return FMLP_ERR_UNSUPPORTED_D;
   if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
   if (workspace_bytes < fmlp_bwd_workspace_size(H, B, D, E, dtype)) return FMLP_ERR_WORKSPACE;
   DeviceInfo* dev = nullptr;
@@ -186,10 +186,12 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
   BwdLaunch a{};
   a.dp = round_dp(D);
   const int bf = dtype == FMLP_DTYPE_BF16;
-  if ((rc = encode3d(&a.tm_x, x, bf, D, B, H, 64, kRows))) return rc;
-  if ((rc = encode3d(&a.tm_do, dO, bf, D, B, H, 64, kRows))) return rc;
+  const int rows = a.dp == 256 ? 64 : kRows;  // B rows and W2 E rows per TMA box
+  if ((rc = encode3d(&a.tm_x, x, bf, D, B, H, 64, rows))) return rc;
+  if ((rc = encode3d(&a.tm_do, dO, bf, D, B, H, 64, rows))) return rc;
   if ((rc = encode3d(&a.tm_w1, w1, bf, E, D, H, 64, a.dp))) return rc;
-  if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, kBwdEt))) return rc;
+  if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, a.dp == 256 ? 64 : kBwdEt))) return rc;
+  a.x = x, a.w1 = w1;
   a.dx = dx, a.dw1 = dw1, a.dw2 = dw2;
   a.H = H, a.B = B, a.D = D, a.E = E;
   a.bf16 = bf;

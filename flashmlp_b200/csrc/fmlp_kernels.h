@@ -22,10 +22,12 @@ struct FwdLaunch {
 };
 
 struct BwdLaunch {
-  CUtensorMap tm_x;    // X  {D, B, H}, box {64, 128, 1}
-  CUtensorMap tm_do;   // dO {D, B, H}, box {64, 128, 1}
+  CUtensorMap tm_x;    // X  {D, B, H}, box {64, 128, 1} (DP = 256: {64, 64, 1})
+  CUtensorMap tm_do;   // dO {D, B, H}, box {64, 128, 1} (DP = 256: {64, 64, 1})
   CUtensorMap tm_w1;   // W1 {E, D, H}, box {64, DP, 1}
-  CUtensorMap tm_w2;   // W2 {D, E, H}, box {64, 128, 1}  (128-row E chunks)
+  CUtensorMap tm_w2;   // W2 {D, E, H}, box {64, 128, 1} (DP = 256: {64, 64, 1})
+  const void* x;       // X and W1 as plain pointers (DP = 256 loads them into TMEM)
+  const void* w1;
   void* dx;
   void* dw1;
   void* dw2;
@@ -45,6 +47,8 @@ int fwd_smem_bytes(int dp);
 int bwd_smem_bytes(int dp);
 cudaError_t launch_fwd(const FwdLaunch& a);       // picks the kernel for a.dp
 cudaError_t launch_fwd_pair(const FwdLaunch& a);  // two row tiles per CTA, D <= 128
-cudaError_t launch_bwd(const BwdLaunch& a);
+cudaError_t launch_bwd(const BwdLaunch& a);     // picks the kernel for a.dp
+cudaError_t launch_bwd256(const BwdLaunch& a);  // 128 < D <= 256
+int bwd256_smem_bytes();
 
 }  // namespace fmlp

@@ -35,7 +35,7 @@ extern "C" {
 #define FMLP_OK 0
 #define FMLP_ERR_INVALID_SHAPE 1    /* negative size or size overflow                  */
 #define FMLP_ERR_UNSUPPORTED_DTYPE 2 /* only fp16 and bf16                             */
-#define FMLP_ERR_UNSUPPORTED_D 3    /* D % 16 != 0, or D > 256 (fwd) / D > 128 (bwd)    */
+#define FMLP_ERR_UNSUPPORTED_D 3    /* D % 16 != 0, or D > 256                          */
 #define FMLP_ERR_UNSUPPORTED_E 4    /* E % 8 != 0 (row stride of W1 must be 16 bytes)  */
 #define FMLP_ERR_MISALIGNED 5       /* a pointer is not 16-byte aligned                */
 #define FMLP_ERR_CUDA 6             /* CUDA runtime / launch error                     */
