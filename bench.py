@@ -234,6 +234,9 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms, fwd_avg, bwd_avg = (float(v) for v in t.tolist())
     status = F._lib.lib().fmlp_device_status(1)
+    # fmlp_fwd_*_kernel + fmlp_bwd_kernel, + fmlp_dw_reduce_kernel when the dW programs are
+    # split (the backward then needs a workspace)
+    launches_per_step = 2 + (1 if F._lib.lib().fmlp_bwd_workspace_size(Hl, B, D, E, 1) else 0)
 
     # ---- e2e through the public API with host buffers (pinned), copies inside the timed region
     n_e2e = max(1, min(n, 5))
@@ -320,7 +323,7 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": round(fl_step_total * n_e2e / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n_e2e,
                 "path": "flashmlp_fwd/flashmlp_bwd on tensors copied from pinned host memory, outputs copied back"},
-        "gpu_launches": 2 * n,
+        "gpu_launches": launches_per_step * n,
         "clocks": clocks,
         "device_status": status,
     }

@@ -127,9 +127,10 @@ def flashmlp_bwd(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     dw2 = torch.empty_like(w2)
     L = _lib.lib()
     dt = _dtype_code(x)
-    ws_bytes = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
     with torch.cuda.device(dev):
+        # scratch for the fp32 dW partial sums of split dW programs (0 bytes for most shapes)
+        ws_bytes = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
         stream = torch.cuda.current_stream(dev).cuda_stream
         rc = L.fmlp_bwd(_ptr(x), _ptr(w1), _ptr(w2), _ptr(do), _ptr(dx), _ptr(dw1), _ptr(dw2),
                         _ptr(ws) if ws is not None else None, ws_bytes, H, B, D, E, dt,

@@ -7,6 +7,11 @@
 //     and loop over every B tile of the head (deterministic, no atomics on outputs);
 //   * dX programs, one per (head, 128-row B tile): own dX[h,tile,:] and loop over E.
 // All dW programs come first in program-id order so the long ones start first.
+// When a launch has too few dW programs to keep the SMs busy (few heads and E chunks,
+// e.g. 4 heads per GPU when 32 heads are sharded over 8 GPUs), each (head, E chunk) is
+// split into S dW programs over contiguous B ranges; they write fp32 partial sums to the
+// caller's workspace and fmlp_dw_reduce_kernel adds them in the fixed order s = 0..S-1
+// (deterministic, still no atomics).
 // Both recompute Z = X@W1 and H = act(Z) per chunk and form dH = dO@W2^T and
 // dZ = dH * act'(Z) in fp32; H and dZ are rounded to the input dtype before they enter
 // the next products (flashmlp.py:212-235, :294-320).
@@ -96,8 +101,8 @@ __global__ void __launch_bounds__(576, 1)
                     const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_w1,
                     const __grid_constant__ CUtensorMap tm_w2, T* __restrict__ dX,
-                    T* __restrict__ dW1, T* __restrict__ dW2, int H, int B, int D, int E,
-                    uint32_t* status) {
+                    T* __restrict__ dW1, T* __restrict__ dW2, float* __restrict__ part,
+                    int splits, int H, int B, int D, int E, uint32_t* status) {
   using C = BwdCfg<DP>;
   using St = ActState<T, ACT>;
   constexpr int BM = C::BM;
@@ -117,13 +122,18 @@ __global__ void __launch_bounds__(576, 1)
   const int lane = threadIdx.x & 31;
   const int nB = (B + BM - 1) / BM;
   const int nE = (E + C::ET - 1) / C::ET;
-  const bool is_dw = int(blockIdx.x) < H * nE;
-  int h, idx;
+  const int nW = H * nE * splits;  // dW programs: (head, split, E chunk), chunk fastest
+  const bool is_dw = int(blockIdx.x) < nW;
+  int h, idx, bt0 = 0, bt1 = nB, split = 0;
   if (is_dw) {
-    h = blockIdx.x / nE;
-    idx = blockIdx.x % nE;  // E chunk
+    h = blockIdx.x / (nE * splits);
+    const int r = blockIdx.x % (nE * splits);
+    split = r / nE;
+    idx = r % nE;  // E chunk
+    bt0 = int((long long)split * nB / splits);  // this program's B tiles [bt0, bt1)
+    bt1 = int((long long)(split + 1) * nB / splits);
   } else {
-    const int p = blockIdx.x - H * nE;
+    const int p = blockIdx.x - nW;
     h = p / nB;
     idx = p % nB;  // B tile
   }
@@ -232,24 +242,26 @@ __global__ void __launch_bounds__(576, 1)
     uint8_t* sX = smem + C::W_OFF_X;
     uint8_t* sDO = smem + C::W_OFF_DO;
     constexpr int XDS = C::XDS;
+    const int nT = bt1 - bt0;  // B tiles of this program; tile i of the loops is bt0 + i
     if (warp == 0) {
       if (lane == 0) {
         mbar_arrive_expect_tx(in_full, C::W1C_BYTES + C::W2C_BYTES);
         for (int r = 0; r < 2; ++r) tma_load_3d(sW1 + r * DP * 128, &tm_w1, in_full, c * 128 + 64 * r, 0, h);
         for (int r = 0; r < DP / 64; ++r) tma_load_3d(sW2 + r * 128 * 128, &tm_w2, in_full, 64 * r, c * 128, h);
         uint32_t nx = 0, nd = 0;  // X / dO stages issued
-        for (int bt = 0; bt < nB; ++bt) {
-          const int s = bt % XDS;
-          const uint32_t par = ((bt / XDS) & 1) ^ 1;
+        for (int i = 0; i < nT; ++i) {
+          const int s = i % XDS;
+          const uint32_t par = ((i / XDS) & 1) ^ 1;
+          const int row = (bt0 + i) * BM;
           if (!mbar_wait(&ring_empty[s], par, ctx)) break;
           mbar_arrive_expect_tx(&ring_full[s], C::TILE_BYTES);
           for (int r = 0; r < DP / 64; ++r)
-            tma_load_3d(sX + s * C::TILE_BYTES + r * BM * 128, &tm_x, &ring_full[s], 64 * r, bt * BM, h);
+            tma_load_3d(sX + s * C::TILE_BYTES + r * BM * 128, &tm_x, &ring_full[s], 64 * r, row, h);
           ++nx;
           if (!mbar_wait(&w2_empty[s], par, ctx)) break;
           mbar_arrive_expect_tx(&w2_full[s], C::TILE_BYTES);
           for (int r = 0; r < DP / 64; ++r)
-            tma_load_3d(sDO + s * C::TILE_BYTES + r * BM * 128, &tm_do, &w2_full[s], 64 * r, bt * BM, h);
+            tma_load_3d(sDO + s * C::TILE_BYTES + r * BM * 128, &tm_do, &w2_full[s], 64 * r, row, h);
           ++nd;
         }
         mbar_wait(in_full, 0, drain);
@@ -301,14 +313,14 @@ __global__ void __launch_bounds__(576, 1)
       };
       auto wait_x = [&](int bt) { return warp_wait(&ring_full[bt % XDS], (bt / XDS) & 1, ctx); };
       auto wait_do = [&](int bt) { return warp_wait(&w2_full[bt % XDS], (bt / XDS) & 1, ctx); };
-      bool ok = warp_wait(in_full, 0, ctx) && nB > 0 && wait_x(0) && wait_do(0);
+      bool ok = warp_wait(in_full, 0, ctx) && nT > 0 && wait_x(0) && wait_do(0);
       tc_fence_after();
       if (ok) {
         issue_prod(0, 0);
         issue_prod(1, 0);
       }
-      for (int bt = 0; bt < nB && ok; ++bt) {
-        const bool more = bt + 1 < nB;
+      for (int bt = 0; bt < nT && ok; ++bt) {
+        const bool more = bt + 1 < nT;
         if (!(ok = warp_wait(&a_full[0], bt & 1, ctx))) break;  // H^T(bt) packed
         tc_fence_after();
         issue_dw(0, bt);
@@ -338,7 +350,7 @@ __global__ void __launch_bounds__(576, 1)
       const uint32_t zt = tmem + lane_off + C::W_TM_ZT + 32 * j;
       const uint32_t dt = tmem + lane_off + C::W_TM_DHT + 32 * j;
       bool ok = true;
-      for (int bt = 0; bt < nB && ok; ++bt) {
+      for (int bt = 0; bt < nT && ok; ++bt) {
         St st[32];
         if (!(ok = mbar_wait(&p_full[0], bt & 1, ctx))) break;
         tc_fence_after();
@@ -354,34 +366,67 @@ __global__ void __launch_bounds__(576, 1)
         const int e = c * 128 + q * 32 + lane;
         constexpr int OW = DP / 4;  // accumulator columns per warp
         const int col0 = j * OW;
-        // dW1^T rows are E, columns D: dW1[h, d, e]. Lanes hold consecutive e, so each
-        // column d is one coalesced 64-byte store across the warp.
+        if (splits > 1) {
+          // fp32 partial sums of this B range: part[split][0] is dW1 laid out (H, D, E),
+          // part[split][1] is dW2 laid out (H, E, D); fmlp_dw_reduce_kernel adds them.
+          const size_t n = size_t(H) * D * E;
+          float* p1 = part + size_t(split) * 2 * n;
+          float* p2 = p1 + n;
 #pragma unroll
-        for (int u = 0; u < OW / 16; ++u) {
-          uint32_t v[16];
-          tmem_ld16_sync(tmem + lane_off + C::W_TM_DW1 + col0 + 16 * u, v);
-          if (e < E) {
+          for (int u = 0; u < OW / 16; ++u) {
+            uint32_t v[16];
+            tmem_ld16_sync(tmem + lane_off + C::W_TM_DW1 + col0 + 16 * u, v);
+            if (e < E) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int d = col0 + 16 * u + i;
-              if (d < D) {
-                const uint32_t pk = Pack<T>::pack(__uint_as_float(v[i]), 0.f);
-                reinterpret_cast<uint16_t*>(dW1)[(size_t(h) * D + d) * E + e] = uint16_t(pk & 0xFFFFu);
+              for (int i = 0; i < 16; ++i) {
+                const int d = col0 + 16 * u + i;
+                if (d < D) p1[(size_t(h) * D + d) * E + e] = __uint_as_float(v[i]);
               }
             }
           }
-        }
-        T* w2row = dW2 + (size_t(h) * E + e) * D;
 #pragma unroll
-        for (int u = 0; u < OW / 16; ++u) {
-          uint32_t v[16], p[8];
-          tmem_ld16_sync(tmem + lane_off + C::W_TM_DW2 + col0 + 16 * u, v);
-          plain_pack<T, 8>(v, p);
-          const int cc = col0 + 16 * u;
-          if (e < E) {
-            uint4* dst = reinterpret_cast<uint4*>(w2row + cc);
-            if (cc + 8 <= D) dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
-            if (cc + 16 <= D) dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+          for (int u = 0; u < OW / 16; ++u) {
+            uint32_t v[16];
+            tmem_ld16_sync(tmem + lane_off + C::W_TM_DW2 + col0 + 16 * u, v);
+            const int cc = col0 + 16 * u;
+            if (e < E && cc < D) {  // D % 16 == 0: all 16 columns are inside
+              float4* dst = reinterpret_cast<float4*>(p2 + (size_t(h) * E + e) * D + cc);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                     __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            }
+          }
+        } else {
+          // dW1^T rows are E, columns D: dW1[h, d, e]. Lanes hold consecutive e, so each
+          // column d is one coalesced 64-byte store across the warp.
+#pragma unroll
+          for (int u = 0; u < OW / 16; ++u) {
+            uint32_t v[16];
+            tmem_ld16_sync(tmem + lane_off + C::W_TM_DW1 + col0 + 16 * u, v);
+            if (e < E) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int d = col0 + 16 * u + i;
+                if (d < D) {
+                  const uint32_t pk = Pack<T>::pack(__uint_as_float(v[i]), 0.f);
+                  reinterpret_cast<uint16_t*>(dW1)[(size_t(h) * D + d) * E + e] = uint16_t(pk & 0xFFFFu);
+                }
+              }
+            }
+          }
+          T* w2row = dW2 + (size_t(h) * E + e) * D;
+#pragma unroll
+          for (int u = 0; u < OW / 16; ++u) {
+            uint32_t v[16], p[8];
+            tmem_ld16_sync(tmem + lane_off + C::W_TM_DW2 + col0 + 16 * u, v);
+            plain_pack<T, 8>(v, p);
+            const int cc = col0 + 16 * u;
+            if (e < E) {
+              uint4* dst = reinterpret_cast<uint4*>(w2row + cc);
+              if (cc + 8 <= D) dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+              if (cc + 16 <= D) dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+            }
           }
         }
       }
@@ -548,6 +593,29 @@ __global__ void __launch_bounds__(576, 1)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+// dW1 / dW2 of split dW programs: out[i] = round(sum over s = 0..S-1, in that order, of
+// part[s][which][i]) with which = blockIdx.y (0: dW1 (H,D,E), 1: dW2 (H,E,D)); four
+// elements per step (H*D*E is a multiple of 4). HBM-bound: 4*S bytes read, 2 written per
+// element.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    fmlp_dw_reduce_kernel(const float* __restrict__ part, T* __restrict__ dW1, T* __restrict__ dW2,
+                          long long n4, int splits) {
+  const size_t n = size_t(n4) * 4;
+  const float4* src = reinterpret_cast<const float4*>(part + blockIdx.y * n);
+  const size_t stride4 = 2 * size_t(n4);  // float4s between consecutive splits
+  uint2* dst = reinterpret_cast<uint2*>(blockIdx.y ? dW2 : dW1);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    float4 acc = __ldcs(src + i);
+    for (int s = 1; s < splits; ++s) {
+      const float4 v = __ldcs(src + s * stride4 + i);
+      acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+    }
+    dst[i] = make_uint2(Pack<T>::pack(acc.x, acc.y), Pack<T>::pack(acc.z, acc.w));
+  }
+}
+
 template <int DP, typename T, int ACT>
 static cudaError_t launch_bwd_t(const BwdLaunch& a) {
   using C = BwdCfg<DP>;
@@ -556,11 +624,21 @@ static cudaError_t launch_bwd_t(const BwdLaunch& a) {
   if (e != cudaSuccess) return e;
   const int nB = (a.B + kRows - 1) / kRows;
   const int nE = (a.E + C::ET - 1) / C::ET;
-  const long long grid = (long long)a.H * (nE + nB);
+  const int splits = a.splits < 1 ? 1 : a.splits;
+  if (splits > 1 && (a.part == nullptr || splits > nB)) return cudaErrorInvalidValue;
+  const long long grid = (long long)a.H * ((long long)nE * splits + nB);
   if (grid <= 0 || grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   kern<<<unsigned(grid), C::NUM_THREADS, C::SMEM, a.stream>>>(
       a.tm_x, a.tm_do, a.tm_w1, a.tm_w2, reinterpret_cast<T*>(a.dx), reinterpret_cast<T*>(a.dw1),
-      reinterpret_cast<T*>(a.dw2), a.H, a.B, a.D, a.E, a.status);
+      reinterpret_cast<T*>(a.dw2), a.part, splits, a.H, a.B, a.D, a.E, a.status);
+  cudaError_t le = cudaGetLastError();
+  if (le != cudaSuccess || splits == 1) return le;
+  const long long n4 = (long long)a.H * a.D * a.E / 4;  // E % 8 == 0
+  long long blocks = (n4 + 255) / 256;
+  const long long cap = (long long)a.sm_count * 4;
+  if (blocks > cap) blocks = cap;
+  fmlp_dw_reduce_kernel<T><<<dim3(unsigned(blocks), 2), 256, 0, a.stream>>>(
+      a.part, reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), n4, splits);
   return cudaGetLastError();
 }
 
@@ -577,6 +655,26 @@ static cudaError_t launch_bwd_act(const BwdLaunch& a) {
 template <int DP>
 static cudaError_t launch_bwd_dt(const BwdLaunch& a) {
   return a.bf16 ? launch_bwd_act<DP, __nv_bfloat16>(a) : launch_bwd_act<DP, __half>(a);
+}
+
+int bwd_dw_splits(int H, int B, int D, int E, int sm_count) {
+  if (D > 128 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 1;
+  const long long nB = (B + kRows - 1) / kRows, nE = (E + kBwdEt - 1) / kBwdEt;
+  // Work in units of one 128x128x128 product: a dW program does 4 per B tile, a dX
+  // program 3 per E chunk. Split until one dW program is at most 0.8 of an SM's share of
+  // the launch, keeping at least 2 B tiles per split and at most 8 splits.
+  const long long work = 7LL * H * nE * nB;
+  const long long max_s = nB / 2 < 8 ? nB / 2 : 8;
+  for (long long s = 1; s <= max_s; ++s) {
+    const long long lw = 4 * ((nB + s - 1) / s);
+    if (5 * lw * sm_count <= 4 * work) return int(s);
+  }
+  return max_s < 1 ? 1 : int(max_s);
+}
+
+size_t bwd_workspace_bytes(int H, int B, int D, int E, int sm_count) {
+  const int s = bwd_dw_splits(H, B, D, E, sm_count);
+  return s > 1 ? size_t(2) * s * size_t(H) * D * E * sizeof(float) : 0;
 }
 
 int bwd_smem_bytes(int dp) {

@@ -158,21 +158,24 @@ int fmlp_fwd(const void* x, const void* w1, const void* w2, void* o, int H, int 
 }
 
 size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {
-  (void)H, (void)B, (void)D, (void)E, (void)dtype;
-  return 0;
+  if (check_common(H, B, D, E, dtype) || D % 16 != 0 || D > 256 || E % 8 != 0) return 0;
+  DeviceInfo* dev = nullptr;
+  if (device_info(&dev)) return 0;
+  return bwd_workspace_bytes(H, B, D, E, dev->sm_count);
 }
 
 int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1,
              void* dw2, void* workspace, size_t workspace_bytes, int H, int B, int D, int E,
              int dtype, int act, void* stream) {
-  (void)workspace;
   int rc = check_common(H, B, D, E, dtype);
   if (rc) return rc;
   if (D % 16 != 0 || D > 256) return FMLP_ERR_UNSUPPORTED_D;
   if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
-  if (workspace_bytes < fmlp_bwd_workspace_size(H, B, D, E, dtype)) return FMLP_ERR_WORKSPACE;
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
+  const size_t ws_need = bwd_workspace_bytes(H, B, D, E, dev->sm_count);
+  if (workspace_bytes < ws_need || (ws_need && (workspace == nullptr || !aligned16(workspace))))
+    return FMLP_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (H == 0 || D == 0) return FMLP_OK;
   if (E == 0) return cuda_rc(cudaMemsetAsync(dx, 0, size_t(H) * B * D * 2, st));
@@ -193,6 +196,9 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
   if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, a.dp == 256 ? 64 : kBwdEt))) return rc;
   a.x = x, a.w1 = w1;
   a.dx = dx, a.dw1 = dw1, a.dw2 = dw2;
+  a.splits = ws_need ? bwd_dw_splits(H, B, D, E, dev->sm_count) : 1;
+  a.part = ws_need ? static_cast<float*>(workspace) : nullptr;
+  a.sm_count = dev->sm_count;
   a.H = H, a.B = B, a.D = D, a.E = E;
   a.bf16 = bf;
   a.act = act;

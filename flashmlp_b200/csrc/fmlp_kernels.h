@@ -31,6 +31,9 @@ struct BwdLaunch {
   void* dx;
   void* dw1;
   void* dw2;
+  float* part;         // fp32 dW partial sums of split dW programs (splits > 1), else null
+  int splits;          // dW programs per (head, E chunk); 1 = no split (DP <= 128 only)
+  int sm_count;
   int H, B, D, E;
   int dp, bf16, act;
   uint32_t* status;
@@ -50,5 +53,9 @@ cudaError_t launch_fwd_pair(const FwdLaunch& a);  // two row tiles per CTA, D <=
 cudaError_t launch_bwd(const BwdLaunch& a);     // picks the kernel for a.dp
 cudaError_t launch_bwd256(const BwdLaunch& a);  // 128 < D <= 256
 int bwd256_smem_bytes();
+// Split factor of the dW programs for a backward launch (1 = none) and the fp32 workspace
+// bytes it needs: 2 * splits * H * D * E * 4 when splits > 1.
+int bwd_dw_splits(int H, int B, int D, int E, int sm_count);
+size_t bwd_workspace_bytes(int H, int B, int D, int E, int sm_count);
 
 }  // namespace fmlp

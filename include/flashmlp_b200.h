@@ -41,7 +41,8 @@ extern "C" {
 #define FMLP_ERR_CUDA 6             /* CUDA runtime / launch error                     */
 #define FMLP_ERR_TMA 7              /* tensor-map encoding failed                      */
 #define FMLP_ERR_DEVICE 8           /* current device is not an sm_100 (B200) GPU       */
-#define FMLP_ERR_WORKSPACE 9        /* workspace smaller than fmlp_bwd_workspace_size  */
+#define FMLP_ERR_WORKSPACE 9        /* workspace smaller than fmlp_bwd_workspace_size,
+                                       null or not 16-byte aligned                     */
 #define FMLP_ERR_DEVICE_TIMEOUT 10  /* a kernel's bounded pipeline wait ran out        */
 
 /*
@@ -61,8 +62,12 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
              void* dw2, void* workspace, size_t workspace_bytes, int H, int B, int D, int E,
              int dtype, int act, void* stream);
 
-/* Device scratch bytes fmlp_bwd needs for this shape (no reference counterpart; the
- * reference allocates its outputs with torch.zeros_like, flashmlp.py:516-518). */
+/* Device scratch bytes fmlp_bwd needs for this shape on the current device (no reference
+ * counterpart; the reference allocates its outputs with torch.zeros_like,
+ * flashmlp.py:516-518). Nonzero only when the launch has too few (head, E chunk) pairs to
+ * fill the GPU (e.g. 4 heads with E = 2048 on a 148-SM B200): the dW programs are then
+ * split over B ranges and their fp32 partial sums (2 * splits * H * D * E floats) are added
+ * in a fixed order by a second kernel. Returns 0 for invalid arguments. */
 size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype);
 
 /*

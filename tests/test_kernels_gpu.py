@@ -133,6 +133,72 @@ def test_d256_vs_oracle():
                 np.testing.assert_allclose(a, r, atol=atol, rtol=rtol, err_msg=f"{shape} {act} {name}")
 
 
+# ----------------------------------------------------------------------------- split dW programs
+def _ws_bytes(H, B, D, E, dt):
+    from flashmlp_b200 import _lib
+    code = _lib.FMLP_DTYPE_BF16 if dt == torch.bfloat16 else _lib.FMLP_DTYPE_F16
+    return int(_lib.lib().fmlp_bwd_workspace_size(H, B, D, E, code))
+
+
+@pytest.mark.parametrize("shape,dtype", [((2, 1000, 96, 200), "bf16"), ((1, 2048, 128, 256), "f16"),
+                                         ((3, 1100, 64, 520), "bf16"), ((2, 4096, 16, 136), "f16")])
+def test_split_dw_vs_oracle(shape, dtype):
+    # Few (head, E chunk) pairs: the dW programs are split over B ranges and their fp32
+    # partials reduced by a second kernel; ragged B (1000, 1100) ends inside the last split.
+    from oracle import flashmlp_oracle as orc
+
+    H, B, D, E = shape
+    dt = _torch_dtype(dtype)
+    assert _ws_bytes(H, B, D, E, dt) > 0, "shape chosen to exercise split dW programs"
+    xs = orc.make_inputs(H, B, D, E, dtype, seed=B + E)
+    x, w1, w2, do = (torch.from_numpy(a).to(dt).cuda() for a in xs)
+    atol, rtol = tol_for(dt, "bwd")
+    for act in ACTS:
+        got = [to_np(t) for t in F().flashmlp_bwd(x, w1, w2, do, act)]
+        want = orc.bwd_kernel(*xs, act, dtype)
+        for name, a, r in zip(("dx", "dw1", "dw2"), got, want):
+            np.testing.assert_allclose(a, r, atol=atol, rtol=rtol, err_msg=f"{shape} {act} {name}")
+
+
+def test_split_dw_matches_unsplit_launch():
+    # The same two heads computed alone (dW split 8 ways) and inside a 16-head launch (no
+    # split): dX is bit-identical (the dX programs do not depend on the split); dW differs
+    # only by the order of fp32 additions over B.
+    H, B, D, E = 16, 8192, 128, 1024
+    dt = torch.bfloat16
+    assert _ws_bytes(2, B, D, E, dt) > 0 and _ws_bytes(H, B, D, E, dt) == 0
+    x, w1, w2, do = make_inputs(H, B, D, E, dt, seed=21)
+    big = F().flashmlp_bwd(x, w1, w2, do, "silu")
+    small = F().flashmlp_bwd(x[:2].contiguous(), w1[:2].contiguous(), w2[:2].contiguous(),
+                             do[:2].contiguous(), "silu")
+    assert torch.equal(big[0][:2], small[0])
+    refs = ref_bwd(x[:2], w1[:2], w2[:2], do[:2], "silu")
+    for k, i in (("dw1", 1), ("dw2", 2)):
+        assert_close(small[i], big[i][:2].float(), refs[k][1], dt, "bwd", k)
+        assert_close(small[i], *refs[k], dt, "bwd", k)
+
+
+def test_workspace_too_small_is_rejected():
+    from flashmlp_b200 import _lib
+    import ctypes
+
+    H, B, D, E = 2, 2048, 128, 512
+    dt = torch.bfloat16
+    need = _ws_bytes(H, B, D, E, dt)
+    assert need > 0
+    x, w1, w2, do = make_inputs(H, B, D, E, dt, seed=5)
+    outs = [torch.empty_like(t) for t in (x, w1, w2)]
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    L = _lib.lib()
+    args = [p(x), p(w1), p(w2), p(do), *map(p, outs)]
+    assert L.fmlp_bwd(*args, p(ws), need - 16, H, B, D, E, 1, 2, None) == 9  # FMLP_ERR_WORKSPACE
+    assert L.fmlp_bwd(*args, None, need, H, B, D, E, 1, 2, None) == 9
+    assert L.fmlp_bwd(*args, p(ws), need, H, B, D, E, 1, 2, None) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(outs[1], F().flashmlp_bwd(x, w1, w2, do, "silu")[1])
+
+
 # ----------------------------------------------------------------------------- BASELINE configs
 CONFIGS = {
     # name: (H, B, D, E, dtype, activations)
@@ -140,6 +206,8 @@ CONFIGS = {
     "C2": (16, 16384, 128, 512, torch.bfloat16, ["leaky_relu"]),
     "C3": (12, 1000, 96, 3000, torch.bfloat16, ["", "sigmoid"]),
     "C4": (32, 65536, 128, 2048, torch.bfloat16, ["silu"]),
+    # C4 head-sharded over 8 GPUs: the per-GPU launch (4 heads) splits its dW programs
+    "C4_per_gpu_at_8": (4, 65536, 128, 2048, torch.bfloat16, ["silu"]),
     "C5": (8, 131072, 256, 1024, torch.float16, ["sigmoid"]),
 }
 
