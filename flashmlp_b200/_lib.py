@@ -22,6 +22,7 @@ FMLP_OK = 0
 FMLP_ERR_UNSUPPORTED_D = 3
 FMLP_ERR_UNSUPPORTED_E = 4
 FMLP_ERR_DEVICE_TIMEOUT = 10
+FMLP_ERR_SCRATCH_LIMIT = 11
 
 # Every symbol the header declares, with (restype, argtypes).
 _c_int, _c_vp, _c_sz = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
@@ -33,6 +34,11 @@ SIGNATURES = {
          _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp],
     ),
     "fmlp_bwd_workspace_size": (_c_sz, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "fmlp_bwd_noalloc": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
+         _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp],
+    ),
     "fmlp_sgd_update": (_c_int, [_c_vp, _c_vp, ctypes.c_longlong, ctypes.c_float, _c_int, _c_vp]),
     "fmlp_device_status": (_c_int, [_c_int]),
     "fmlp_error_string": (ctypes.c_char_p, [_c_int]),

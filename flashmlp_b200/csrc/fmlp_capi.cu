@@ -122,6 +122,9 @@ const char* fmlp_error_string(int code) {
     case FMLP_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case FMLP_ERR_WORKSPACE: return "workspace too small";
     case FMLP_ERR_DEVICE_TIMEOUT: return "a kernel pipeline wait timed out on the device";
+    case FMLP_ERR_SCRATCH_LIMIT:
+      return "shape needs more scratch than fmlp_bwd_noalloc's static device buffer "
+             "(FMLP_NOALLOC_SCRATCH_BYTES); call fmlp_bwd with a workspace";
   }
   return "unknown error";
 }

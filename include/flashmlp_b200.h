@@ -44,6 +44,8 @@ extern "C" {
 #define FMLP_ERR_WORKSPACE 9        /* workspace smaller than fmlp_bwd_workspace_size,
                                        null or not 16-byte aligned                     */
 #define FMLP_ERR_DEVICE_TIMEOUT 10  /* a kernel's bounded pipeline wait ran out        */
+#define FMLP_ERR_SCRATCH_LIMIT 11   /* fmlp_bwd_noalloc: shape needs more scratch than
+                                       FMLP_NOALLOC_SCRATCH_BYTES                      */
 
 /*
  * Forward. Replaces flashmlp_fwd + flashmlp_fwd_kernel (flashmlp.py:428-477, :63-158).
@@ -69,6 +71,25 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
  * split over B ranges and their fp32 partial sums (2 * splits * H * D * E floats) are added
  * in a fixed order by a second kernel. Returns 0 for invalid arguments. */
 size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype);
+
+/*
+ * Unified backward that allocates nothing: same arguments and results as fmlp_bwd, minus
+ * the workspace. No counterpart in the reference. It is for callers that cannot allocate
+ * device memory: engines whose memory planner gives a custom operator only its inputs and
+ * outputs, or processes whose allocator already holds the GPU's memory. The fp32 dW
+ * partial sums that fmlp_bwd keeps in the caller's workspace live instead in a static
+ * device array of FMLP_NOALLOC_SCRATCH_BYTES, which every GPU that loads the library holds
+ * until the process exits; a shape whose fmlp_bwd_workspace_size exceeds it returns
+ * FMLP_ERR_SCRATCH_LIMIT (no D <= 256 shape does on a 148-SM B200).
+ * The first call on a device whose shape needs scratch looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream capture on the
+ * device. All calls on a device share the array: calls whose kernels overlap on the GPU
+ * (e.g. on two streams) race on it, so serialise them. It calls no cudaMalloc/cudaFree.
+ */
+#define FMLP_NOALLOC_SCRATCH_BYTES (32u << 20)
+int fmlp_bwd_noalloc(const void* x, const void* w1, const void* w2, const void* dO, void* dx,
+                     void* dw1, void* dw2, int H, int B, int D, int E, int dtype, int act,
+                     void* stream);
 
 /*
  * In-place SGD step w[i] -= lr * g[i] for n elements, g in fp32 (e.g. the all-reduced

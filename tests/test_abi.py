@@ -42,7 +42,7 @@ def test_python_constants_match_header():
 def test_error_strings_and_version():
     L = _lib.lib()
     assert L.fmlp_abi_version() == 100
-    for code in range(0, 11):
+    for code in range(0, 12):
         s = L.fmlp_error_string(code).decode()
         assert s and s != "unknown error"
     assert L.fmlp_error_string(99).decode() == "unknown error"
@@ -62,6 +62,7 @@ def test_argument_validation_without_device():
     assert L.fmlp_sgd_update(nul, nul, -5, 0.1, 1, nul) == d["FMLP_ERR_INVALID_SHAPE"]
     assert L.fmlp_sgd_update(nul, nul, 5, 0.1, 3, nul) == d["FMLP_ERR_UNSUPPORTED_DTYPE"]
     assert L.fmlp_bwd_workspace_size(32, 65536, 128, 2048, 1) == 0
+    assert L.fmlp_bwd_noalloc(nul, nul, nul, nul, nul, nul, nul, 1, 128, 272, 64, 1, 0, nul) == d["FMLP_ERR_UNSUPPORTED_D"]
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
