@@ -5,7 +5,7 @@ flashmlp_bwd, FlashMLPFunction, FlashMLP, plus the plain-PyTorch PyTorchMLP,
 flashmlp_torch_fwd and flashmlp_torch_bwd it also exports. Multi-GPU wrappers live in
 flashmlp_b200.sharding.
 """
-from .api import FlashMLP, FlashMLPFunction, activation_code, flashmlp_bwd, flashmlp_fwd
+from .api import FlashMLP, FlashMLPFunction, activation_code, flashmlp_bwd, flashmlp_bwd_dw_f32, flashmlp_fwd
 from .torch_reference import PyTorchMLP, flashmlp_torch_bwd, flashmlp_torch_fwd
 from ._lib import FlashMLPError
 
@@ -19,4 +19,5 @@ __all__ = [
     "flashmlp_torch_bwd",
     "FlashMLPError",
     "activation_code",
+    "flashmlp_bwd_dw_f32",
 ]

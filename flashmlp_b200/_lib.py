@@ -23,6 +23,8 @@ FMLP_ERR_UNSUPPORTED_D = 3
 FMLP_ERR_UNSUPPORTED_E = 4
 FMLP_ERR_DEVICE_TIMEOUT = 10
 FMLP_ERR_SCRATCH_LIMIT = 11
+FMLP_MAX_PEERS = 8
+FMLP_IPC_HANDLE_BYTES = 64
 
 # Every symbol the header declares, with (restype, argtypes).
 _c_int, _c_vp, _c_sz = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
@@ -39,7 +41,22 @@ SIGNATURES = {
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
          _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp],
     ),
+    "fmlp_bwd_dw_f32": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_sz,
+         _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp],
+    ),
     "fmlp_sgd_update": (_c_int, [_c_vp, _c_vp, ctypes.c_longlong, ctypes.c_float, _c_int, _c_vp]),
+    "fmlp_grad_allreduce_sgd": (
+        _c_int,
+        [ctypes.POINTER(_c_vp), ctypes.POINTER(_c_vp), ctypes.POINTER(_c_vp), _c_int, _c_int,
+         ctypes.c_longlong, ctypes.c_float, _c_int, ctypes.c_uint, _c_vp],
+    ),
+    "fmlp_peer_alloc": (_c_int, [_c_sz, ctypes.POINTER(_c_vp)]),
+    "fmlp_peer_free": (_c_int, [_c_vp]),
+    "fmlp_ipc_get_handle": (_c_int, [_c_vp, _c_vp]),
+    "fmlp_ipc_open_handle": (_c_int, [_c_vp, ctypes.POINTER(_c_vp)]),
+    "fmlp_ipc_close_handle": (_c_int, [_c_vp]),
     "fmlp_device_status": (_c_int, [_c_int]),
     "fmlp_error_string": (ctypes.c_char_p, [_c_int]),
     "fmlp_abi_version": (_c_int, []),

@@ -139,6 +139,44 @@ def flashmlp_bwd(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     return dx.reshape(H, B, D), dw1.reshape(H, D, E), dw2.reshape(H, E, D)
 
 
+def flashmlp_bwd_dw_f32(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, do: torch.Tensor,
+                        activation: str = "", dw_out: torch.Tensor = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Backward with dW as unrounded fp32 sums over this call's rows (fmlp_bwd_dw_f32).
+
+    Returns (dx, dw) with dx like flashmlp_bwd's and dw a flat fp32 tensor holding dW1
+    (H, D, E) followed by dW2 (H, E, D); `dw_out` (2*H*D*E fp32, contiguous) is filled
+    instead of a new tensor when given. Used by the batch-sharded step, whose ranks add
+    their fp32 partials before any rounding."""
+    assert x.shape[2] == w1.shape[1], "Hidden dimension mismatch"
+    assert w1.shape[2] == w2.shape[1], "Intermediate dimension mismatch"
+    assert x.shape[2] == w2.shape[2], "Output dimension mismatch"
+    assert x.shape == do.shape, "Gradient shape mismatch"
+    H, B, D = x.shape
+    E = w1.shape[2]
+    x = x.contiguous()
+    w1 = w1.contiguous()
+    w2 = w2.contiguous()
+    do = do.contiguous()
+    dev = _check_tensors(x, w1, w2, do)
+    dx = torch.empty_like(x)
+    n = 2 * H * D * E
+    if dw_out is None:
+        dw_out = torch.empty(n, dtype=torch.float32, device=dev)
+    elif dw_out.dtype != torch.float32 or dw_out.numel() != n or not dw_out.is_contiguous() or dw_out.device != dev:
+        raise ValueError(f"dw_out must be a contiguous float32 tensor of {n} elements on {dev}")
+    L = _lib.lib()
+    dt = _dtype_code(x)
+    with torch.cuda.device(dev):
+        ws_bytes = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = L.fmlp_bwd_dw_f32(_ptr(x), _ptr(w1), _ptr(w2), _ptr(do), _ptr(dx), _ptr(dw_out),
+                               _ptr(ws) if ws is not None else None, ws_bytes, H, B, D, E, dt,
+                               activation_code(activation), ctypes.c_void_p(stream))
+    _lib.check(rc, "fmlp_bwd_dw_f32")
+    return dx, dw_out
+
+
 class FlashMLPFunction(torch.autograd.Function):
     """Autograd wrapper; saves only X, W1 and W2 (flashmlp.py:545-557)."""
 

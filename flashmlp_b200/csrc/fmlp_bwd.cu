@@ -366,9 +366,10 @@ __global__ void __launch_bounds__(576, 1)
         const int e = c * 128 + q * 32 + lane;
         constexpr int OW = DP / 4;  // accumulator columns per warp
         const int col0 = j * OW;
-        if (splits > 1) {
-          // fp32 partial sums of this B range: part[split][0] is dW1 laid out (H, D, E),
-          // part[split][1] is dW2 laid out (H, E, D); fmlp_dw_reduce_kernel adds them.
+        if (part != nullptr) {
+          // fp32 sums of this B range: part[split][0] is dW1 laid out (H, D, E),
+          // part[split][1] is dW2 laid out (H, E, D); with several splits
+          // fmlp_dw_reduce_kernel adds them, with one it is the fp32 output itself.
           const size_t n = size_t(H) * D * E;
           float* p1 = part + size_t(split) * 2 * n;
           float* p2 = p1 + n;
@@ -593,18 +594,20 @@ __global__ void __launch_bounds__(576, 1)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
-// dW1 / dW2 of split dW programs: out[i] = round(sum over s = 0..S-1, in that order, of
-// part[s][which][i]) with which = blockIdx.y (0: dW1 (H,D,E), 1: dW2 (H,E,D)); four
-// elements per step (H*D*E is a multiple of 4). HBM-bound: 4*S bytes read, 2 written per
+// dW1 / dW2 of split dW programs: out[i] = sum over s = 0..S-1, in that order, of
+// part[s][which][i] with which = blockIdx.y (0: dW1 (H,D,E), 1: dW2 (H,E,D)), rounded into
+// dW1 / dW2, or stored unrounded into out_f32[which][i] when out_f32 is set; four elements
+// per step (H*D*E is a multiple of 4). HBM-bound: 4*S bytes read, 2 (or 4) written per
 // element.
 template <typename T>
 __global__ void __launch_bounds__(256)
     fmlp_dw_reduce_kernel(const float* __restrict__ part, T* __restrict__ dW1, T* __restrict__ dW2,
-                          long long n4, int splits) {
+                          float* __restrict__ out_f32, long long n4, int splits) {
   const size_t n = size_t(n4) * 4;
   const float4* src = reinterpret_cast<const float4*>(part + blockIdx.y * n);
   const size_t stride4 = 2 * size_t(n4);  // float4s between consecutive splits
   uint2* dst = reinterpret_cast<uint2*>(blockIdx.y ? dW2 : dW1);
+  float4* dstf = out_f32 ? reinterpret_cast<float4*>(out_f32 + blockIdx.y * n) : nullptr;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
        i += (long long)gridDim.x * blockDim.x) {
     float4 acc = __ldcs(src + i);
@@ -612,7 +615,10 @@ __global__ void __launch_bounds__(256)
       const float4 v = __ldcs(src + s * stride4 + i);
       acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
     }
-    dst[i] = make_uint2(Pack<T>::pack(acc.x, acc.y), Pack<T>::pack(acc.z, acc.w));
+    if (dstf)
+      dstf[i] = acc;
+    else
+      dst[i] = make_uint2(Pack<T>::pack(acc.x, acc.y), Pack<T>::pack(acc.z, acc.w));
   }
 }
 
@@ -628,9 +634,11 @@ static cudaError_t launch_bwd_t(const BwdLaunch& a) {
   if (splits > 1 && (a.part == nullptr || splits > nB)) return cudaErrorInvalidValue;
   const long long grid = (long long)a.H * ((long long)nE * splits + nB);
   if (grid <= 0 || grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
+  // the dW programs' fp32 target: the split partials, or the fp32 output itself
+  float* kpart = splits > 1 ? a.part : a.dw_f32;
   kern<<<unsigned(grid), C::NUM_THREADS, C::SMEM, a.stream>>>(
       a.tm_x, a.tm_do, a.tm_w1, a.tm_w2, reinterpret_cast<T*>(a.dx), reinterpret_cast<T*>(a.dw1),
-      reinterpret_cast<T*>(a.dw2), a.part, splits, a.H, a.B, a.D, a.E, a.status);
+      reinterpret_cast<T*>(a.dw2), kpart, splits, a.H, a.B, a.D, a.E, a.status);
   cudaError_t le = cudaGetLastError();
   if (le != cudaSuccess || splits == 1) return le;
   const long long n4 = (long long)a.H * a.D * a.E / 4;  // E % 8 == 0
@@ -638,7 +646,7 @@ static cudaError_t launch_bwd_t(const BwdLaunch& a) {
   const long long cap = (long long)a.sm_count * 4;
   if (blocks > cap) blocks = cap;
   fmlp_dw_reduce_kernel<T><<<dim3(unsigned(blocks), 2), 256, 0, a.stream>>>(
-      a.part, reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), n4, splits);
+      a.part, reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), a.dw_f32, n4, splits);
   return cudaGetLastError();
 }
 

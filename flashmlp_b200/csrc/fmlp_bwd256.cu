@@ -82,7 +82,8 @@ __global__ void __launch_bounds__(576, 1)
                        const __grid_constant__ CUtensorMap tm_w1,
                        const __grid_constant__ CUtensorMap tm_w2, const T* __restrict__ X,
                        const T* __restrict__ W1, T* __restrict__ dX, T* __restrict__ dW1,
-                       T* __restrict__ dW2, int H, int B, int D, int E, uint32_t* status) {
+                       T* __restrict__ dW2, float* __restrict__ dwf, int H, int B, int D, int E,
+                       uint32_t* status) {
   using C = Bwd256Cfg;
   using St = ActState<T, ACT>;
   constexpr int DP = C::DP;
@@ -341,34 +342,65 @@ __global__ void __launch_bounds__(576, 1)
         tc_fence_after();
         const int e = c * C::EW + q * 32 + lane;
         const int d0 = g * 128 + 32 * j;  // this warp's 32 accumulator columns
-        // dW1^T rows are E, columns D: dW1[h, d, e]; lanes hold consecutive e, so each
-        // column d is one coalesced 64-byte store across the warp.
+        if (dwf != nullptr) {
+          // unrounded fp32 output: dW1 laid out (H, D, E), then dW2 laid out (H, E, D)
+          float* f1 = dwf;
+          float* f2 = dwf + size_t(H) * D * E;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          uint32_t v[16];
-          tmem_ld16_sync(tmem + lane_off + C::W_TM_DW1 + 32 * j + 16 * u, v);
-          if (e < E) {
+          for (int u = 0; u < 2; ++u) {
+            uint32_t v[16];
+            tmem_ld16_sync(tmem + lane_off + C::W_TM_DW1 + 32 * j + 16 * u, v);
+            if (e < E) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int d = d0 + 16 * u + i;
-              if (d < D) {
-                const uint32_t pk = Pack<T>::pack(__uint_as_float(v[i]), 0.f);
-                reinterpret_cast<uint16_t*>(dW1)[(size_t(h) * D + d) * E + e] = uint16_t(pk & 0xFFFFu);
+              for (int i = 0; i < 16; ++i) {
+                const int d = d0 + 16 * u + i;
+                if (d < D) f1[(size_t(h) * D + d) * E + e] = __uint_as_float(v[i]);
               }
             }
           }
-        }
-        T* w2row = dW2 + (size_t(h) * E + e) * D;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          uint32_t v[16], p[8];
-          tmem_ld16_sync(tmem + lane_off + C::W_TM_DW2 + 32 * j + 16 * u, v);
-          plain_pack<T, 8>(v, p);
-          const int cc = d0 + 16 * u;
-          if (e < E) {
-            uint4* dst = reinterpret_cast<uint4*>(w2row + cc);
-            if (cc + 8 <= D) dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
-            if (cc + 16 <= D) dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+          for (int u = 0; u < 2; ++u) {
+            uint32_t v[16];
+            tmem_ld16_sync(tmem + lane_off + C::W_TM_DW2 + 32 * j + 16 * u, v);
+            const int cc = d0 + 16 * u;
+            if (e < E && cc < D) {  // D % 16 == 0: all 16 columns are inside
+              float4* dst = reinterpret_cast<float4*>(f2 + (size_t(h) * E + e) * D + cc);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                     __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            }
+          }
+        } else {
+          // dW1^T rows are E, columns D: dW1[h, d, e]; lanes hold consecutive e, so each
+          // column d is one coalesced 64-byte store across the warp.
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            uint32_t v[16];
+            tmem_ld16_sync(tmem + lane_off + C::W_TM_DW1 + 32 * j + 16 * u, v);
+            if (e < E) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int d = d0 + 16 * u + i;
+                if (d < D) {
+                  const uint32_t pk = Pack<T>::pack(__uint_as_float(v[i]), 0.f);
+                  reinterpret_cast<uint16_t*>(dW1)[(size_t(h) * D + d) * E + e] = uint16_t(pk & 0xFFFFu);
+                }
+              }
+            }
+          }
+          T* w2row = dW2 + (size_t(h) * E + e) * D;
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            uint32_t v[16], p[8];
+            tmem_ld16_sync(tmem + lane_off + C::W_TM_DW2 + 32 * j + 16 * u, v);
+            plain_pack<T, 8>(v, p);
+            const int cc = d0 + 16 * u;
+            if (e < E) {
+              uint4* dst = reinterpret_cast<uint4*>(w2row + cc);
+              if (cc + 8 <= D) dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+              if (cc + 16 <= D) dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+            }
           }
         }
       }
@@ -549,8 +581,8 @@ static cudaError_t launch_bwd256_t(const BwdLaunch& a) {
   if (grid <= 0 || grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   kern<<<unsigned(grid), C::NUM_THREADS, C::SMEM, a.stream>>>(
       a.tm_x, a.tm_do, a.tm_w1, a.tm_w2, reinterpret_cast<const T*>(a.x), reinterpret_cast<const T*>(a.w1),
-      reinterpret_cast<T*>(a.dx), reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), a.H, a.B, a.D, a.E,
-      a.status);
+      reinterpret_cast<T*>(a.dx), reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), a.dw_f32, a.H, a.B,
+      a.D, a.E, a.status);
   return cudaGetLastError();
 }
 

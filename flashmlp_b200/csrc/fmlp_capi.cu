@@ -88,18 +88,30 @@ int round_dp(int D) { return D <= 64 ? 64 : (D <= 128 ? 128 : 256); }
 
 int cuda_rc(cudaError_t e) { return e == cudaSuccess ? FMLP_OK : FMLP_ERR_CUDA; }
 
+// w - lr * g is formed with two roundings (no FMA contraction), the same arithmetic as the
+// fused all-reduce + SGD kernel and as `w.float() - lr * g` in PyTorch.
 __global__ void sgd_kernel_bf16(__nv_bfloat16* w, const float* g, long long n, float lr) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x)
-    w[i] = __float2bfloat16_rn(__bfloat162float(w[i]) - lr * g[i]);
+    w[i] = __float2bfloat16_rn(__fsub_rn(__bfloat162float(w[i]), __fmul_rn(lr, g[i])));
 }
 __global__ void sgd_kernel_f16(__half* w, const float* g, long long n, float lr) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x)
-    w[i] = __float2half_rn(__half2float(w[i]) - lr * g[i]);
+    w[i] = __float2half_rn(__fsub_rn(__half2float(w[i]), __fmul_rn(lr, g[i])));
 }
 
 }  // namespace
+
+int current_device_status(int* sm_count, uint32_t** status) {
+  DeviceInfo* d = nullptr;
+  const int rc = device_info(&d);
+  if (rc) return rc;
+  *sm_count = d->sm_count;
+  *status = d->status;
+  return FMLP_OK;
+}
+
 }  // namespace fmlp
 
 using namespace fmlp;
@@ -167,9 +179,15 @@ size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {
   return bwd_workspace_bytes(H, B, D, E, dev->sm_count);
 }
 
-int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1,
-             void* dw2, void* workspace, size_t workspace_bytes, int H, int B, int D, int E,
-             int dtype, int act, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Shared body of fmlp_bwd (dW rounded into dw1/dw2) and fmlp_bwd_dw_f32 (dW as unrounded
+// fp32 into dwf = dW1 (H,D,E) followed by dW2 (H,E,D)).
+int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1, void* dw2,
+             float* dwf, void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype, int act,
+             void* stream) {
   int rc = check_common(H, B, D, E, dtype);
   if (rc) return rc;
   if (D % 16 != 0 || D > 256) return FMLP_ERR_UNSUPPORTED_D;
@@ -183,12 +201,13 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
   if (H == 0 || D == 0) return FMLP_OK;
   if (E == 0) return cuda_rc(cudaMemsetAsync(dx, 0, size_t(H) * B * D * 2, st));
   if (B == 0) {
+    if (dwf) return cuda_rc(cudaMemsetAsync(dwf, 0, size_t(2) * H * D * E * sizeof(float), st));
     if ((rc = cuda_rc(cudaMemsetAsync(dw1, 0, size_t(H) * D * E * 2, st)))) return rc;
     return cuda_rc(cudaMemsetAsync(dw2, 0, size_t(H) * E * D * 2, st));
   }
-  if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(dO) || !aligned16(dx) ||
-      !aligned16(dw1) || !aligned16(dw2))
+  if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(dO) || !aligned16(dx))
     return FMLP_ERR_MISALIGNED;
+  if (dwf ? !aligned16(dwf) : (!aligned16(dw1) || !aligned16(dw2))) return FMLP_ERR_MISALIGNED;
   BwdLaunch a{};
   a.dp = round_dp(D);
   const int bf = dtype == FMLP_DTYPE_BF16;
@@ -199,6 +218,7 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
   if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, a.dp == 256 ? 64 : kBwdEt))) return rc;
   a.x = x, a.w1 = w1;
   a.dx = dx, a.dw1 = dw1, a.dw2 = dw2;
+  a.dw_f32 = dwf;
   a.splits = ws_need ? bwd_dw_splits(H, B, D, E, dev->sm_count) : 1;
   a.part = ws_need ? static_cast<float*>(workspace) : nullptr;
   a.sm_count = dev->sm_count;
@@ -208,6 +228,24 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
   a.status = dev->status;
   a.stream = st;
   return cuda_rc(launch_bwd(a));
+}
+
+}  // namespace
+
+extern "C" {
+
+int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1,
+             void* dw2, void* workspace, size_t workspace_bytes, int H, int B, int D, int E,
+             int dtype, int act, void* stream) {
+  return bwd_impl(x, w1, w2, dO, dx, dw1, dw2, nullptr, workspace, workspace_bytes, H, B, D, E, dtype, act,
+                  stream);
+}
+
+int fmlp_bwd_dw_f32(const void* x, const void* w1, const void* w2, const void* dO, void* dx, float* dw_f32,
+                    void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype, int act,
+                    void* stream) {
+  return bwd_impl(x, w1, w2, dO, dx, nullptr, nullptr, dw_f32, workspace, workspace_bytes, H, B, D, E, dtype,
+                  act, stream);
 }
 
 int fmlp_sgd_update(void* w, const float* g, long long n, float lr, int dtype, void* stream) {

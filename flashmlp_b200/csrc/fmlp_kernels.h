@@ -32,6 +32,7 @@ struct BwdLaunch {
   void* dw1;
   void* dw2;
   float* part;         // fp32 dW partial sums of split dW programs (splits > 1), else null
+  float* dw_f32;       // if set: dW1 (H,D,E) then dW2 (H,E,D) as unrounded fp32, not dw1/dw2
   int splits;          // dW programs per (head, E chunk); 1 = no split (DP <= 128 only)
   int sm_count;
   int H, B, D, E;
@@ -53,6 +54,9 @@ cudaError_t launch_fwd_pair(const FwdLaunch& a);  // two row tiles per CTA, D <=
 cudaError_t launch_bwd(const BwdLaunch& a);     // picks the kernel for a.dp
 cudaError_t launch_bwd256(const BwdLaunch& a);  // 128 < D <= 256
 int bwd256_smem_bytes();
+// SM count and device status word of the current device (fails if it is not an sm_100).
+int current_device_status(int* sm_count, uint32_t** status);
+
 // Split factor of the dW programs for a backward launch (1 = none) and the fp32 workspace
 // bytes it needs: 2 * splits * H * D * E * 4 when splits > 1.
 int bwd_dw_splits(int H, int B, int D, int E, int sm_count);

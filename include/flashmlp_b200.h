@@ -64,6 +64,17 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
              void* dw2, void* workspace, size_t workspace_bytes, int H, int B, int D, int E,
              int dtype, int act, void* stream);
 
+/*
+ * The same backward with dW left as unrounded fp32 sums over this call's B rows:
+ * dw_f32 holds dW1 laid out (H,D,E) followed by dW2 laid out (H,E,D), 2*H*D*E floats.
+ * dx is written as in fmlp_bwd; the workspace rule is fmlp_bwd's. Used by the batch-
+ * sharded step, whose ranks add their fp32 partials before rounding (no reference
+ * counterpart: flashmlp.py:480-538 returns dW in the input dtype).
+ */
+int fmlp_bwd_dw_f32(const void* x, const void* w1, const void* w2, const void* dO, void* dx,
+                    float* dw_f32, void* workspace, size_t workspace_bytes, int H, int B, int D,
+                    int E, int dtype, int act, void* stream);
+
 /* Device scratch bytes fmlp_bwd needs for this shape on the current device (no reference
  * counterpart; the reference allocates its outputs with torch.zeros_like,
  * flashmlp.py:516-518). Nonzero only when the launch has too few (head, E chunk) pairs to
@@ -97,6 +108,37 @@ int fmlp_bwd_noalloc(const void* x, const void* w1, const void* w2, const void* 
  * the reference has no optimizer (no counterpart).
  */
 int fmlp_sgd_update(void* w, const float* g, long long n, float lr, int dtype, void* stream);
+
+/*
+ * Fused gradient all-reduce + SGD of the batch-sharded training step over NVLink peer
+ * memory; no reference counterpart (it replaces an NCCL all-reduce of dW1 || dW2 followed
+ * by fmlp_sgd_update). One process per GPU, world <= FMLP_MAX_PEERS ranks on distinct GPUs
+ * of one node. peer_w[k] (n 16-bit weights, rank k's replica), peer_g[k] (n fp32
+ * gradients of rank k's rows) and peer_flags[k] (world uint32 counters, zero-initialised)
+ * are rank k's buffers as mapped into this process (fmlp_ipc_open_handle; the own rank's
+ * entries are its plain device pointers); the arrays themselves are host memory. Every
+ * rank calls with the same n, lr, dtype and epoch, and a fresh epoch per call (two
+ * counter values are used per call: epoch and epoch + 1). Rank r sums slice r of the
+ * gradients over ranks 0..world-1 in that order in fp32, applies w = round(w - lr * g) and
+ * stores the result into every replica; barriers before and after make every replica
+ * complete when the call's work on `stream` ends. A peer that does not arrive within the
+ * wait limit leaves FMLP_ERR_DEVICE_TIMEOUT in fmlp_device_status. n % 4 == 0.
+ */
+#define FMLP_MAX_PEERS 8
+int fmlp_grad_allreduce_sgd(void* const* peer_w, const float* const* peer_g,
+                            uint32_t* const* peer_flags, int world, int rank, long long n, float lr,
+                            int dtype, unsigned epoch, void* stream);
+
+/* CUDA IPC plumbing for the buffers above (no reference counterpart). fmlp_peer_alloc
+ * returns a zeroed cudaMalloc allocation of its own, so its IPC handle maps exactly that
+ * buffer; fmlp_ipc_get_handle writes FMLP_IPC_HANDLE_BYTES bytes that another process on
+ * the same node passes to fmlp_ipc_open_handle to map the buffer. */
+#define FMLP_IPC_HANDLE_BYTES 64
+int fmlp_peer_alloc(size_t bytes, void** dev_ptr);
+int fmlp_peer_free(void* dev_ptr);
+int fmlp_ipc_get_handle(const void* dev_ptr, void* handle);
+int fmlp_ipc_open_handle(const void* handle, void** dev_ptr);
+int fmlp_ipc_close_handle(void* dev_ptr);
 
 /* Reads the current device's kernel status word (FMLP_OK or FMLP_ERR_DEVICE_TIMEOUT),
  * optionally clearing it. Synchronises the device. */

@@ -178,6 +178,25 @@ def test_split_dw_matches_unsplit_launch():
         assert_close(small[i], *refs[k], dt, "bwd", k)
 
 
+@pytest.mark.parametrize("shape,dtype", [((4, 4096, 128, 1024), torch.bfloat16), ((16, 8192, 128, 1024), torch.bfloat16),
+                                         ((2, 1000, 256, 520), torch.float16), ((3, 700, 64, 200), torch.float16)])
+def test_bwd_dw_f32_rounds_to_bwd(shape, dtype):
+    # The fp32-dW backward is the same computation: rounding its dW gives fmlp_bwd's dW bit
+    # for bit, and dX is identical (split and unsplit dW programs, D <= 128 and D = 256).
+    H, B, D, E = shape
+    x, w1, w2, do = make_inputs(H, B, D, E, dtype, seed=13)
+    for act in ("silu", "leaky_relu"):
+        dx, dw1, dw2 = F().flashmlp_bwd(x, w1, w2, do, act)
+        dxf, dwf = F().flashmlp_bwd_dw_f32(x, w1, w2, do, act)
+        n1 = H * D * E
+        assert torch.equal(dx, dxf)
+        assert torch.equal(dwf[:n1].view(H, D, E).to(dtype), dw1)
+        assert torch.equal(dwf[n1:].view(H, E, D).to(dtype), dw2)
+    x, w1, w2, do = make_inputs(H, 0, D, E, dtype)
+    _, dwf = F().flashmlp_bwd_dw_f32(x, w1, w2, do, "silu", dw_out=torch.full((2 * H * D * E,), 7.0, device="cuda"))
+    assert torch.count_nonzero(dwf) == 0
+
+
 def test_workspace_too_small_is_rejected():
     from flashmlp_b200 import _lib
     import ctypes

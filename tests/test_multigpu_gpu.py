@@ -81,6 +81,50 @@ def _batch_case(rank, world):
     return e1 <= 0, e2 <= 0, same, moved
 
 
+def _fused_case(rank, world):
+    """Two steps of the fused batch-sharded trainer against the same arithmetic done with
+    NCCL: fp32 partial gradients summed in rank order, then w - lr * g rounded once."""
+    import torch.distributed as dist
+
+    import flashmlp_b200 as F
+    from flashmlp_b200 import sharding
+
+    dev = torch.device("cuda", rank)
+    results = []
+    for (H, B, D, E, dt, act) in ((4, 2048, 128, 512, torch.bfloat16, "silu"),
+                                  (2, 1000, 256, 264, torch.float16, "sigmoid")):
+        x, w1, w2, do = (t.to(dev) for t in _inputs(H, B, D, E, dt, seed=5))
+        xl, dol = sharding.shard_batch(x, world, rank), sharding.shard_batch(do, world, rank)
+        tr = sharding.FusedBatchShardedTrainer(w1, w2)
+        rw1, rw2 = w1.clone(), w2.clone()
+        ok = True
+        for step, lr in enumerate((0.05, 0.02)):
+            # reference arithmetic on this rank, with NCCL moving the partials
+            ro = F.flashmlp_fwd(xl, rw1, rw2, act)
+            rdx, part = F.flashmlp_bwd_dw_f32(xl, rw1, rw2, dol, act)
+            parts = [torch.empty_like(part) for _ in range(world)]
+            dist.all_gather(parts, part)
+            g = parts[0].clone()
+            for p_ in parts[1:]:
+                g += p_
+            n1 = rw1.numel()
+            rw1 = (rw1.float() - lr * g[:n1].view(rw1.shape)).to(dt)
+            rw2 = (rw2.float() - lr * g[n1:].view(rw2.shape)).to(dt)
+            o, dx = tr.step(xl, dol, act, lr)
+            torch.cuda.synchronize()
+            ok &= torch.equal(o, ro) and torch.equal(dx, rdx)
+            ok &= torch.equal(tr.w1, rw1) and torch.equal(tr.w2, rw2)
+            ws = torch.cat([tr.w1.reshape(-1), tr.w2.reshape(-1)]).float()
+            gathered = [torch.empty_like(ws) for _ in range(world)]
+            dist.all_gather(gathered, ws)
+            ok &= all(torch.equal(gathered[0], t) for t in gathered[1:])
+        ok &= not torch.equal(tr.w1, w1)
+        ok &= F._lib.lib().fmlp_device_status(1) == 0
+        tr.close()
+        results.append(bool(ok))
+    return results
+
+
 def _worker(rank, world, port, case, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -141,3 +185,12 @@ def test_batch_sharded_step_gradients_and_replicas():
         assert ok1 and ok2, f"rank {rank}: summed gradients outside tolerance (dw1 {ok1}, dw2 {ok2})"
         assert same, f"rank {rank}: replicas differ after the update"
         assert moved, f"rank {rank}: weights not updated"
+
+
+def test_fused_allreduce_sgd_trainer_two_steps():
+    # fmlp_grad_allreduce_sgd over NVLink peer memory: replicas bit-identical and equal to
+    # the fixed-order fp32 sum of the ranks' partial gradients followed by the SGD step
+    _need_two()
+    out = _run(_fused_case)
+    for rank, flags in out.items():
+        assert all(flags), f"rank {rank}: (bf16 D=128, fp16 D=256) cases ok = {flags}"
