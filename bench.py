@@ -331,6 +331,88 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
+C5 = dict(H=8, B=131072, D=256, E=1024, activation="sigmoid", dtype="f16")
+C5_NAME = "C5 batch-sharded training step H=8 B=131072 D=256 E=1024 fp16 sigmoid"
+
+
+def run_c5(args, rank, world, local_rank):
+    """data-parallel training step (fwd + bwd on B/N rows per GPU, dW
+    all-reduce over NVLink, SGD). --allreduce fused: FusedBatchShardedTrainer (fp32 partials,
+    fmlp_grad_allreduce_sgd); nccl: batch_sharded_train_step (NCCL all-reduce + update)."""
+    import torch
+    import torch.distributed as dist
+
+    import flashmlp_b200 as F
+    from flashmlp_b200 import sharding
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29517")
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    H, B, D, E = (C5[k] for k in "HBDE")
+    act, dt, lr = C5["activation"], torch.float16, 1e-4
+    b0, b1 = sharding.shard_range(B, world, rank)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(H, b1 - b0, D, device=dev, generator=g).to(dt)
+    do = torch.randn(H, b1 - b0, D, device=dev, generator=g).to(dt)
+    gw = torch.Generator(device=dev).manual_seed(7)  # replicas start equal
+    w1 = (torch.randn(H, D, E, device=dev, generator=gw) / D ** 0.5).to(dt)
+    w2 = (torch.randn(H, E, D, device=dev, generator=gw) / E ** 0.5).to(dt)
+    fused = args.allreduce == "fused"
+    tr = sharding.FusedBatchShardedTrainer(w1, w2) if fused else None
+
+    def step():
+        if fused:
+            tr.step(x, do, act, lr)
+        else:
+            sharding.batch_sharded_train_step(x, do, w1, w2, act, lr)
+
+    for _ in range(args.warmup):
+        step()
+    dist.barrier()
+    torch.cuda.synchronize()
+    n = args.steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(n):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    status = F._lib.lib().fmlp_device_status(1)
+    if tr is not None:
+        tr.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    fl = 12.0 * H * B * D * E
+    line = {
+        "metric": METRIC, "value": round(fl * n / (total_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": round(total_ms / n, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": C5_NAME, "H": H, "B": B, "D": D, "E": E, "activation": act,
+                   "rows_per_gpu": b1 - b0, "parallelism": f"batch-sharded x{world}",
+                   "allreduce": "fused fmlp_grad_allreduce_sgd (NVLink peer memory)" if fused
+                   else "NCCL all-reduce + fmlp_sgd_update",
+                   "l2": "inputs larger than L2 every step; no flush"},
+        "clocks": clocks, "device_status": status,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -338,6 +420,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["c4", "c5"], default="c4",
+                    help="c4 (default, the headline): head-sharded fwd+bwd; c5: batch-sharded training step")
+    ap.add_argument("--allreduce", choices=["fused", "nccl"], default="fused", help="c5 only")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -348,6 +433,8 @@ def main():
         print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.workload == "c5":
+        return run_c5(args, rank, world, local_rank)
     return run_ours(args, rank, world, local_rank)
 
 
