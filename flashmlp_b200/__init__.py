@@ -5,7 +5,8 @@ flashmlp_bwd, FlashMLPFunction, FlashMLP, plus the plain-PyTorch PyTorchMLP,
 flashmlp_torch_fwd and flashmlp_torch_bwd it also exports. Multi-GPU wrappers live in
 flashmlp_b200.sharding.
 """
-from .api import FlashMLP, FlashMLPFunction, activation_code, flashmlp_bwd, flashmlp_bwd_dw_f32, flashmlp_fwd
+from .api import (FlashMLP, FlashMLPFunction, FlashMLPSharedInputFunction, activation_code, flashmlp_bwd,
+                  flashmlp_bwd_dw_f32, flashmlp_bwd_shared_x, flashmlp_fwd, flashmlp_fwd_shared_x)
 from .torch_reference import PyTorchMLP, flashmlp_torch_bwd, flashmlp_torch_fwd
 from ._lib import FlashMLPError
 
@@ -20,4 +21,7 @@ __all__ = [
     "FlashMLPError",
     "activation_code",
     "flashmlp_bwd_dw_f32",
+    "flashmlp_fwd_shared_x",
+    "flashmlp_bwd_shared_x",
+    "FlashMLPSharedInputFunction",
 ]

@@ -41,6 +41,12 @@ SIGNATURES = {
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
          _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp],
     ),
+    "fmlp_fwd_shared_x": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp]),
+    "fmlp_bwd_shared_x": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_sz,
+         _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp],
+    ),
     "fmlp_bwd_dw_f32": (
         _c_int,
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_sz,

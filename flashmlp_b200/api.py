@@ -177,6 +177,74 @@ def flashmlp_bwd_dw_f32(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, do:
     return dx, dw_out
 
 
+def flashmlp_fwd_shared_x(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                          activation: str = "") -> torch.Tensor:
+    """Mean over heads of the MLP of one shared input: x (B, D) -> (B, D),
+    (1/H) * sum_h act(x @ w1[h]) @ w2[h] (fmlp_fwd_shared_x). Equals
+    flashmlp_fwd(x.expand(H, B, D), w1, w2).mean(0) -- the reference's FlashMLP on a 2-D
+    input, flashmlp.py:603-614 -- without materialising the expanded x or the per-head
+    outputs; the head sum is accumulated in fp32 and rounded once. Needs D <= 128."""
+    assert x.dim() == 2 and x.shape[1] == w1.shape[1], "Hidden dimension mismatch"
+    assert w1.shape[0] == w2.shape[0], "Number of heads must match"
+    assert w1.shape[2] == w2.shape[1], "Intermediate dimension mismatch"
+    assert x.shape[1] == w2.shape[2], "Output dimension mismatch"
+    H, D, E = w1.shape
+    B = x.shape[0]
+    x, w1, w2 = x.contiguous(), w1.contiguous(), w2.contiguous()
+    dev = _check_tensors(x, w1, w2)
+    o = torch.empty_like(x)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = _lib.lib().fmlp_fwd_shared_x(_ptr(x), _ptr(w1), _ptr(w2), _ptr(o), H, B, D, E, _dtype_code(x),
+                                          activation_code(activation), ctypes.c_void_p(stream))
+    _lib.check(rc, "fmlp_fwd_shared_x")
+    return o
+
+
+def flashmlp_bwd_shared_x(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, do: torch.Tensor,
+                          activation: str = "") -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Backward of flashmlp_fwd_shared_x (fmlp_bwd_shared_x): do (B, D) is the gradient of
+    the head mean; returns dx (B, D) (summed over heads), dw1 (H, D, E), dw2 (H, E, D)."""
+    assert x.dim() == 2 and x.shape == do.shape, "Gradient shape mismatch"
+    assert x.shape[1] == w1.shape[1], "Hidden dimension mismatch"
+    assert w1.shape[2] == w2.shape[1], "Intermediate dimension mismatch"
+    H, D, E = w1.shape
+    B = x.shape[0]
+    x, w1, w2, do = x.contiguous(), w1.contiguous(), w2.contiguous(), do.contiguous()
+    dev = _check_tensors(x, w1, w2, do)
+    dx = torch.empty_like(x)
+    dw1 = torch.empty_like(w1)
+    dw2 = torch.empty_like(w2)
+    L = _lib.lib()
+    dt = _dtype_code(x)
+    with torch.cuda.device(dev):
+        ws_bytes = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = L.fmlp_bwd_shared_x(_ptr(x), _ptr(w1), _ptr(w2), _ptr(do), _ptr(dx), _ptr(dw1), _ptr(dw2),
+                                 _ptr(ws) if ws is not None else None, ws_bytes, H, B, D, E, dt,
+                                 activation_code(activation), ctypes.c_void_p(stream))
+    _lib.check(rc, "fmlp_bwd_shared_x")
+    return dx, dw1, dw2
+
+
+class FlashMLPSharedInputFunction(torch.autograd.Function):
+    """Autograd for the head mean of a shared (B, D) input; saves only x, W1 and W2."""
+
+    @staticmethod
+    def forward(ctx, x, w1, w2, activation=""):
+        o = flashmlp_fwd_shared_x(x, w1, w2, activation)
+        ctx.save_for_backward(x, w1, w2)
+        ctx.activation = activation
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        x, w1, w2 = ctx.saved_tensors
+        dx, dw1, dw2 = flashmlp_bwd_shared_x(x, w1, w2, do, ctx.activation)
+        return dx, dw1, dw2, None
+
+
 class FlashMLPFunction(torch.autograd.Function):
     """Autograd wrapper; saves only X, W1 and W2 (flashmlp.py:545-557)."""
 
@@ -199,7 +267,10 @@ class FlashMLP(torch.nn.Module):
 
     Parameters `w1` (H, D, E) and `w2` (H, E, D) are initialised like the reference,
     randn / sqrt(E) and randn / sqrt(D), so state dicts interchange. A 2-D input (B, D) is
-    broadcast to every head and the output is averaged over heads.
+    broadcast to every head and the output is averaged over heads; for D <= 128 this runs
+    on the shared-input kernels (no (H, B, D) copies of x, dO or dX; the head mean is
+    accumulated in fp32), for larger D on the per-head kernels with the expanded input,
+    as in the reference (flashmlp.py:603-614).
     """
 
     def __init__(self, num_heads: int, hidden_dim: int, intermediate_dim: int,
@@ -220,6 +291,8 @@ class FlashMLP(torch.nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         squeeze_output = x.dim() == 2
+        if squeeze_output and x.shape[-1] <= 128 and self.num_heads > 0:
+            return FlashMLPSharedInputFunction.apply(x, self.w1, self.w2, self.activation)
         if squeeze_output:
             x = x.unsqueeze(0).expand(self.num_heads, -1, -1)
         o = FlashMLPFunction.apply(x, self.w1, self.w2, self.activation)

@@ -12,6 +12,12 @@
 // split into S dW programs over contiguous B ranges; they write fp32 partial sums to the
 // caller's workspace and fmlp_dw_reduce_kernel adds them in the fixed order s = 0..S-1
 // (deterministic, still no atomics).
+// With SX (shared input: X, dO and dX are (B, D) matrices used by every head, the
+// backward of the reference's FlashMLP on a 2-D input, flashmlp.py:603-614), the dW
+// programs read the shared X/dO tiles, there is one dX program per B tile that loops over
+// (head, E chunk) pairs and accumulates dX over all heads in TMEM (the sum the expand's
+// backward takes), and the 1/H of the head mean is applied to dH (and so to dZ and dW1)
+// and to dW2 in fp32.
 // Both recompute Z = X@W1 and H = act(Z) per chunk and form dH = dO@W2^T and
 // dZ = dH * act'(Z) in fp32; H and dZ are rounded to the input dtype before they enter
 // the next products (flashmlp.py:212-235, :294-320).
@@ -95,7 +101,7 @@ struct BwdCfg {
   static constexpr int NUM_THREADS = 32 * (FIRST_ACT_WARP + NUM_ACT_WARPS);
 };
 
-template <int DP, typename T, int ACT>
+template <int DP, typename T, int ACT, bool SX>
 __global__ void __launch_bounds__(576, 1)
     fmlp_bwd_kernel(const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_do,
@@ -123,6 +129,9 @@ __global__ void __launch_bounds__(576, 1)
   const int nB = (B + BM - 1) / BM;
   const int nE = (E + C::ET - 1) / C::ET;
   const int nW = H * nE * splits;  // dW programs: (head, split, E chunk), chunk fastest
+  // dX programs loop over E chunks of their head, or (SX) over (head, E chunk) pairs
+  const int nEv = SX ? H * nE : nE;
+  const float inv_h = SX ? 1.0f / float(H) : 1.0f;
   const bool is_dw = int(blockIdx.x) < nW;
   int h, idx, bt0 = 0, bt1 = nB, split = 0;
   if (is_dw) {
@@ -134,8 +143,8 @@ __global__ void __launch_bounds__(576, 1)
     bt1 = int((long long)(split + 1) * nB / splits);
   } else {
     const int p = blockIdx.x - nW;
-    h = p / nB;
-    idx = p % nB;  // B tile
+    h = SX ? 0 : p / nB;  // SX: one program per B tile for all heads
+    idx = SX ? p : p % nB;  // B tile
   }
 
   // Every barrier below completes at most one phase ahead of each of its waiters, so
@@ -205,6 +214,12 @@ __global__ void __launch_bounds__(576, 1)
                                st[17 + 2 * i]);
     if (pack_h) tmem_st8(col + 8, ph);
   };
+  // dH as phase 2 uses it: with a shared input the upstream gradient of the head mean is
+  // dO / H, applied here in fp32 (dH is linear in dO).
+  auto dh_in = [&](uint32_t v) -> float {
+    if constexpr (SX) return __uint_as_float(v) * inv_h;
+    return __uint_as_float(v);
+  };
   // Phase 2 over the 32 dH columns at `src`: dZ packed into the 16 columns at `dst`
   // (`dst` == `src`, or columns this warp has already read in phase 1).
   auto phase2 = [&](uint32_t src, uint32_t dst, const St (&st)[32]) {
@@ -214,12 +229,12 @@ __global__ void __launch_bounds__(576, 1)
     tmem_ld16_async(src + 16, vb);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      pd[i] = grad_pair<T, ACT>(__uint_as_float(va[2 * i]), __uint_as_float(va[2 * i + 1]), st[2 * i], st[2 * i + 1]);
+      pd[i] = grad_pair<T, ACT>(dh_in(va[2 * i]), dh_in(va[2 * i + 1]), st[2 * i], st[2 * i + 1]);
     tmem_st8(dst, pd);
     tmem_wait_ld_dep(vb);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      pd[i] = grad_pair<T, ACT>(__uint_as_float(vb[2 * i]), __uint_as_float(vb[2 * i + 1]), st[16 + 2 * i],
+      pd[i] = grad_pair<T, ACT>(dh_in(vb[2 * i]), dh_in(vb[2 * i + 1]), st[16 + 2 * i],
                                 st[17 + 2 * i]);
     tmem_st8(dst + 8, pd);
   };
@@ -256,12 +271,12 @@ __global__ void __launch_bounds__(576, 1)
           if (!mbar_wait(&ring_empty[s], par, ctx)) break;
           mbar_arrive_expect_tx(&ring_full[s], C::TILE_BYTES);
           for (int r = 0; r < DP / 64; ++r)
-            tma_load_3d(sX + s * C::TILE_BYTES + r * BM * 128, &tm_x, &ring_full[s], 64 * r, row, h);
+            tma_load_3d(sX + s * C::TILE_BYTES + r * BM * 128, &tm_x, &ring_full[s], 64 * r, row, SX ? 0 : h);
           ++nx;
           if (!mbar_wait(&w2_empty[s], par, ctx)) break;
           mbar_arrive_expect_tx(&w2_full[s], C::TILE_BYTES);
           for (int r = 0; r < DP / 64; ++r)
-            tma_load_3d(sDO + s * C::TILE_BYTES + r * BM * 128, &tm_do, &w2_full[s], 64 * r, row, h);
+            tma_load_3d(sDO + s * C::TILE_BYTES + r * BM * 128, &tm_do, &w2_full[s], 64 * r, row, SX ? 0 : h);
           ++nd;
         }
         mbar_wait(in_full, 0, drain);
@@ -366,6 +381,14 @@ __global__ void __launch_bounds__(576, 1)
         const int e = c * 128 + q * 32 + lane;
         constexpr int OW = DP / 4;  // accumulator columns per warp
         const int col0 = j * OW;
+        // dW2 = H^T dO_h with dO_h = dO / H for a shared input (dW1 already carries 1/H
+        // through dZ)
+        auto scale_dw2 = [&](uint32_t (&v)[16]) {
+          if constexpr (SX) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * inv_h);
+          }
+        };
         if (part != nullptr) {
           // fp32 sums of this B range: part[split][0] is dW1 laid out (H, D, E),
           // part[split][1] is dW2 laid out (H, E, D); with several splits
@@ -389,6 +412,7 @@ __global__ void __launch_bounds__(576, 1)
           for (int u = 0; u < OW / 16; ++u) {
             uint32_t v[16];
             tmem_ld16_sync(tmem + lane_off + C::W_TM_DW2 + col0 + 16 * u, v);
+            scale_dw2(v);
             const int cc = col0 + 16 * u;
             if (e < E && cc < D) {  // D % 16 == 0: all 16 columns are inside
               float4* dst = reinterpret_cast<float4*>(p2 + (size_t(h) * E + e) * D + cc);
@@ -421,6 +445,7 @@ __global__ void __launch_bounds__(576, 1)
           for (int u = 0; u < OW / 16; ++u) {
             uint32_t v[16], p[8];
             tmem_ld16_sync(tmem + lane_off + C::W_TM_DW2 + col0 + 16 * u, v);
+            scale_dw2(v);
             plain_pack<T, 8>(v, p);
             const int cc = col0 + 16 * u;
             if (e < E) {
@@ -453,7 +478,7 @@ __global__ void __launch_bounds__(576, 1)
           if (!mbar_wait(&ring_empty[s], ((c / C::WS1) & 1) ^ 1, ctx)) return false;
           mbar_arrive_expect_tx(&ring_full[s], C::W1C_BYTES);
           for (int r = 0; r < 2; ++r)
-            tma_load_3d(sW1 + s * C::W1C_BYTES + r * DP * 128, &tm_w1, &ring_full[s], c * 128 + 64 * r, 0, h);
+            tma_load_3d(sW1 + s * C::W1C_BYTES + r * DP * 128, &tm_w1, &ring_full[s], (c % nE) * 128 + 64 * r, 0, SX ? c / nE : h);
           ++n1;
           return true;
         };
@@ -462,11 +487,11 @@ __global__ void __launch_bounds__(576, 1)
           if (!mbar_wait(&w2_empty[s], ((c / C::WS2) & 1) ^ 1, ctx)) return false;
           mbar_arrive_expect_tx(&w2_full[s], C::W2C_BYTES);
           for (int r = 0; r < DP / 64; ++r)
-            tma_load_3d(sW2 + s * C::W2C_BYTES + r * 128 * 128, &tm_w2, &w2_full[s], 64 * r, c * 128, h);
+            tma_load_3d(sW2 + s * C::W2C_BYTES + r * 128 * 128, &tm_w2, &w2_full[s], 64 * r, (c % nE) * 128, SX ? c / nE : h);
           ++n2;
           return true;
         };
-        for (int c = 0; c < nE; ++c)
+        for (int c = 0; c < nEv; ++c)
           if (!load_w1(c) || !load_w2(c)) break;
         mbar_wait(in_full, 0, drain);
         for (uint32_t s = 0; s < C::WS1; ++s)
@@ -507,21 +532,21 @@ __global__ void __launch_bounds__(576, 1)
       };
       auto wait_w1 = [&](int c) { return warp_wait(&ring_full[c % C::WS1], (c / C::WS1) & 1, ctx); };
       auto wait_w2 = [&](int c) { return warp_wait(&w2_full[c % C::WS2], (c / C::WS2) & 1, ctx); };
-      bool ok = warp_wait(in_full, 0, ctx) && nE > 0 && wait_w1(0) && wait_w2(0);
+      bool ok = warp_wait(in_full, 0, ctx) && nEv > 0 && wait_w1(0) && wait_w2(0);
       tc_fence_after();
       if (ok) {
         issue_z(0);
         issue_dh(0);
-        if (nE > 1 && (ok = wait_w1(1))) {
+        if (nEv > 1 && (ok = wait_w1(1))) {
           tc_fence_after();
           issue_z(1);
         }
       }
-      for (int c = 0; c < nE && ok; ++c) {
+      for (int c = 0; c < nEv && ok; ++c) {
         // Phase 2(c) has read dH(c) and packed dZ(c) over the Z(c) buffer.
         if (!(ok = warp_wait(&a_full[1], c & 1, ctx))) break;
         tc_fence_after();
-        if (c + 1 < nE) {
+        if (c + 1 < nEv) {
           if (!(ok = wait_w2(c + 1))) break;
           tc_fence_after();
           issue_dh(c + 1);
@@ -538,7 +563,7 @@ __global__ void __launch_bounds__(576, 1)
           mma_commit(&ring_empty[s]);  // dX(c) is the W1c stage's last reader
         }
         __syncwarp();
-        if (c + 2 < nE) {  // overwrites dZ(c) after dX(c) read it
+        if (c + 2 < nEv) {  // overwrites dZ(c) after dX(c) read it
           if (!(ok = wait_w1(c + 2))) break;
           tc_fence_after();
           issue_z(c + 2);
@@ -555,7 +580,7 @@ __global__ void __launch_bounds__(576, 1)
       // Per E chunk: E columns [32j, 32j+32) of Z (buffer c%2) and dH.
       const uint32_t da = tmem + lane_off + C::X_TM_DH + 32 * j;
       bool ok = true;
-      for (int c = 0; c < nE && ok; ++c) {
+      for (int c = 0; c < nEv && ok; ++c) {
         St st[32];
         const uint32_t zc = tmem + lane_off + C::X_TM_Z + (c & 1) * 128 + 32 * j;
         if (!(ok = mbar_wait(&p_full[(c & 1) ? 2 : 0], (c >> 1) & 1, ctx))) break;
@@ -622,17 +647,17 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-template <int DP, typename T, int ACT>
-static cudaError_t launch_bwd_t(const BwdLaunch& a) {
+template <int DP, typename T, int ACT, bool SX>
+static cudaError_t launch_bwd_sx(const BwdLaunch& a) {
   using C = BwdCfg<DP>;
-  auto kern = fmlp_bwd_kernel<DP, T, ACT>;
+  auto kern = fmlp_bwd_kernel<DP, T, ACT, SX>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int nB = (a.B + kRows - 1) / kRows;
   const int nE = (a.E + C::ET - 1) / C::ET;
   const int splits = a.splits < 1 ? 1 : a.splits;
   if (splits > 1 && (a.part == nullptr || splits > nB)) return cudaErrorInvalidValue;
-  const long long grid = (long long)a.H * ((long long)nE * splits + nB);
+  const long long grid = (long long)a.H * nE * splits + (SX ? 1LL : (long long)a.H) * nB;
   if (grid <= 0 || grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   // the dW programs' fp32 target: the split partials, or the fp32 output itself
   float* kpart = splits > 1 ? a.part : a.dw_f32;
@@ -648,6 +673,11 @@ static cudaError_t launch_bwd_t(const BwdLaunch& a) {
   fmlp_dw_reduce_kernel<T><<<dim3(unsigned(blocks), 2), 256, 0, a.stream>>>(
       a.part, reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), a.dw_f32, n4, splits);
   return cudaGetLastError();
+}
+
+template <int DP, typename T, int ACT>
+static cudaError_t launch_bwd_t(const BwdLaunch& a) {
+  return a.shared_x ? launch_bwd_sx<DP, T, ACT, true>(a) : launch_bwd_sx<DP, T, ACT, false>(a);
 }
 
 template <int DP, typename T>
@@ -698,7 +728,7 @@ cudaError_t launch_bwd(const BwdLaunch& a) {
   switch (a.dp) {
     case 64: return launch_bwd_dt<64>(a);
     case 128: return launch_bwd_dt<128>(a);
-    case 256: return launch_bwd256(a);
+    case 256: return a.shared_x ? cudaErrorNotSupported : launch_bwd256(a);
   }
   return cudaErrorNotSupported;
 }

@@ -126,7 +126,7 @@ const char* fmlp_error_string(int code) {
     case FMLP_ERR_INVALID_SHAPE: return "invalid shape (negative size or too large)";
     case FMLP_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype (only float16 and bfloat16)";
     case FMLP_ERR_UNSUPPORTED_D:
-      return "unsupported hidden dim D (needs D % 16 == 0 and D <= 256)";
+      return "unsupported hidden dim D (needs D % 16 == 0 and D <= 256; D <= 128 for the shared-input entry points)";
     case FMLP_ERR_UNSUPPORTED_E: return "unsupported intermediate dim E (needs E % 8 == 0)";
     case FMLP_ERR_MISALIGNED: return "tensor data pointer is not 16-byte aligned";
     case FMLP_ERR_CUDA: return "CUDA runtime error";
@@ -141,35 +141,58 @@ const char* fmlp_error_string(int code) {
   return "unknown error";
 }
 
-int fmlp_fwd(const void* x, const void* w1, const void* w2, void* o, int H, int B, int D, int E,
-             int dtype, int act, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Shared body of fmlp_fwd (X, O per head) and fmlp_fwd_shared_x (X, O (B,D), O the mean
+// over heads).
+int fwd_impl(const void* x, const void* w1, const void* w2, void* o, int H, int B, int D, int E, int dtype,
+             int act, int shared_x, void* stream) {
   int rc = check_common(H, B, D, E, dtype);
   if (rc) return rc;
-  if (D % 16 != 0 || D > 256) return FMLP_ERR_UNSUPPORTED_D;
+  if (D % 16 != 0 || D > (shared_x ? 128 : 256)) return FMLP_ERR_UNSUPPORTED_D;
   if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
+  if (shared_x && H == 0) return FMLP_ERR_INVALID_SHAPE;  // no mean over zero heads
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if ((long long)H * B * D == 0) return FMLP_OK;
-  if (E == 0) return cuda_rc(cudaMemsetAsync(o, 0, size_t(H) * B * D * 2, st));
+  const size_t o_elems = size_t(shared_x ? 1 : H) * B * D;
+  if (o_elems == 0) return FMLP_OK;
+  if (E == 0) return cuda_rc(cudaMemsetAsync(o, 0, o_elems * 2, st));
   if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(o)) return FMLP_ERR_MISALIGNED;
   FwdLaunch a{};
   a.dp = round_dp(D);
   const int et = fwd_et(a.dp);
   const int bf = dtype == FMLP_DTYPE_BF16;
-  if ((rc = encode3d(&a.tm_x, x, bf, D, B, H, 64, kRows))) return rc;
+  if ((rc = encode3d(&a.tm_x, x, bf, D, B, shared_x ? 1 : H, 64, kRows))) return rc;
   if ((rc = encode3d(&a.tm_w1, w1, bf, E, D, H, 64, a.dp))) return rc;
   if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, et))) return rc;
   a.o = o;
   a.H = H, a.B = B, a.D = D, a.E = E;
   a.bf16 = bf;
   a.act = act;
+  a.shared_x = shared_x;
   const long long tiles = (long long)H * ((B + kRows - 1) / kRows);
   a.grid = int(tiles < dev->sm_count ? tiles : dev->sm_count);
   a.sm_count = dev->sm_count;
   a.status = dev->status;
   a.stream = st;
   return cuda_rc(launch_fwd(a));
+}
+
+}  // namespace
+
+extern "C" {
+
+int fmlp_fwd(const void* x, const void* w1, const void* w2, void* o, int H, int B, int D, int E,
+             int dtype, int act, void* stream) {
+  return fwd_impl(x, w1, w2, o, H, B, D, E, dtype, act, 0, stream);
+}
+
+int fmlp_fwd_shared_x(const void* x, const void* w1, const void* w2, void* o, int H, int B, int D, int E,
+                      int dtype, int act, void* stream) {
+  return fwd_impl(x, w1, w2, o, H, B, D, E, dtype, act, 1, stream);
 }
 
 size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {
@@ -187,11 +210,12 @@ namespace {
 // fp32 into dwf = dW1 (H,D,E) followed by dW2 (H,E,D)).
 int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1, void* dw2,
              float* dwf, void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype, int act,
-             void* stream) {
+             int shared_x, void* stream) {
   int rc = check_common(H, B, D, E, dtype);
   if (rc) return rc;
-  if (D % 16 != 0 || D > 256) return FMLP_ERR_UNSUPPORTED_D;
+  if (D % 16 != 0 || D > (shared_x ? 128 : 256)) return FMLP_ERR_UNSUPPORTED_D;
   if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
+  if (shared_x && H == 0) return FMLP_ERR_INVALID_SHAPE;
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
   const size_t ws_need = bwd_workspace_bytes(H, B, D, E, dev->sm_count);
@@ -199,7 +223,7 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
     return FMLP_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (H == 0 || D == 0) return FMLP_OK;
-  if (E == 0) return cuda_rc(cudaMemsetAsync(dx, 0, size_t(H) * B * D * 2, st));
+  if (E == 0) return cuda_rc(cudaMemsetAsync(dx, 0, size_t(shared_x ? 1 : H) * B * D * 2, st));
   if (B == 0) {
     if (dwf) return cuda_rc(cudaMemsetAsync(dwf, 0, size_t(2) * H * D * E * sizeof(float), st));
     if ((rc = cuda_rc(cudaMemsetAsync(dw1, 0, size_t(H) * D * E * 2, st)))) return rc;
@@ -212,8 +236,9 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
   a.dp = round_dp(D);
   const int bf = dtype == FMLP_DTYPE_BF16;
   const int rows = a.dp == 256 ? 64 : kRows;  // B rows and W2 E rows per TMA box
-  if ((rc = encode3d(&a.tm_x, x, bf, D, B, H, 64, rows))) return rc;
-  if ((rc = encode3d(&a.tm_do, dO, bf, D, B, H, 64, rows))) return rc;
+  const int hx = shared_x ? 1 : H;  // heads of X / dO
+  if ((rc = encode3d(&a.tm_x, x, bf, D, B, hx, 64, rows))) return rc;
+  if ((rc = encode3d(&a.tm_do, dO, bf, D, B, hx, 64, rows))) return rc;
   if ((rc = encode3d(&a.tm_w1, w1, bf, E, D, H, 64, a.dp))) return rc;
   if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, a.dp == 256 ? 64 : kBwdEt))) return rc;
   a.x = x, a.w1 = w1;
@@ -225,6 +250,7 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
   a.H = H, a.B = B, a.D = D, a.E = E;
   a.bf16 = bf;
   a.act = act;
+  a.shared_x = shared_x;
   a.status = dev->status;
   a.stream = st;
   return cuda_rc(launch_bwd(a));
@@ -237,7 +263,14 @@ extern "C" {
 int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1,
              void* dw2, void* workspace, size_t workspace_bytes, int H, int B, int D, int E,
              int dtype, int act, void* stream) {
-  return bwd_impl(x, w1, w2, dO, dx, dw1, dw2, nullptr, workspace, workspace_bytes, H, B, D, E, dtype, act,
+  return bwd_impl(x, w1, w2, dO, dx, dw1, dw2, nullptr, workspace, workspace_bytes, H, B, D, E, dtype, act, 0,
+                  stream);
+}
+
+int fmlp_bwd_shared_x(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1,
+                      void* dw2, void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype,
+                      int act, void* stream) {
+  return bwd_impl(x, w1, w2, dO, dx, dw1, dw2, nullptr, workspace, workspace_bytes, H, B, D, E, dtype, act, 1,
                   stream);
 }
 
@@ -245,7 +278,7 @@ int fmlp_bwd_dw_f32(const void* x, const void* w1, const void* w2, const void* d
                     void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype, int act,
                     void* stream) {
   return bwd_impl(x, w1, w2, dO, dx, nullptr, nullptr, dw_f32, workspace, workspace_bytes, H, B, D, E, dtype,
-                  act, stream);
+                  act, 0, stream);
 }
 
 int fmlp_sgd_update(void* w, const float* g, long long n, float lr, int dtype, void* stream) {

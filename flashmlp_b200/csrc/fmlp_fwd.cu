@@ -390,7 +390,7 @@ cudaError_t launch_fwd(const FwdLaunch& a) {
   switch (a.dp) {
     case 64:
     case 128: return launch_fwd_pair(a);
-    case 256: return launch_fwd_dt<256>(a);
+    case 256: return a.shared_x ? cudaErrorNotSupported : launch_fwd_dt<256>(a);
   }
   return cudaErrorInvalidValue;
 }

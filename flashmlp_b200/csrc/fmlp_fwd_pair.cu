@@ -15,6 +15,13 @@
 //
 // TMEM (DP=128): O_A [0,128) O_B [128,256) Z_A [256,384) Z_B [384,512).
 // smem: X_A, X_B tiles + 2-stage W1 and W2 rings (DP=64: 4 stages).
+//
+// SX = true (shared input): X is one (B, D) matrix used by every head and the output is
+// the mean over heads, O = (1/H) sum_h act(X @ W1[h]) @ W2[h] -- what the reference's
+// FlashMLP computes for a 2-D input by expanding X to (H, B, D) and averaging the per-head
+// outputs (flashmlp.py:603-614), without the H copies of X and of O. A work item is a
+// pair of row tiles; its chunk loop runs over (head, E chunk), X stays in shared memory
+// for all heads and O accumulates over all heads in TMEM; the epilogue scales by 1/H.
 #include "fmlp_act.cuh"
 #include "fmlp_kernels.h"
 #include "fmlp_ptx.cuh"
@@ -52,7 +59,7 @@ struct FwdPairCfg {
   static constexpr int OW = DP / 4;  // O columns per activation warp
 };
 
-template <int DP, typename T, int ACT>
+template <int DP, typename T, int ACT, bool SX>
 __global__ void __launch_bounds__(608, 1)
     fmlp_fwd_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
                          const __grid_constant__ CUtensorMap tm_w1,
@@ -89,7 +96,8 @@ __global__ void __launch_bounds__(608, 1)
   const int nB = (B + BM - 1) / BM;
   const int nP = (nB + 1) / 2;  // row pairs per head
   const int nE = (E + ET - 1) / ET;
-  const int nitems = H * nP;
+  const int nEv = SX ? H * nE : nE;  // chunks per work item: (head, chunk) pairs when SX
+  const int nitems = SX ? nP : H * nP;
 
   if (threadIdx.x == 0) {
     misc[1] = 0;
@@ -131,7 +139,7 @@ __global__ void __launch_bounds__(608, 1)
       uint32_t xl[2] = {0, 0};          // X loads issued per tile slot
       bool ok = true;
       for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++it) {
-        const int h = item / nP, pr = item % nP;
+        const int h = SX ? 0 : item / nP, pr = SX ? item : item % nP;
         for (int t = 0; t < 2 && ok; ++t) {
           if (!(ok = mbar_wait(&x_empty[t], (it & 1) ^ 1, ctx))) break;
           mbar_arrive_expect_tx(&x_full[t], C::X_BYTES);
@@ -140,13 +148,15 @@ __global__ void __launch_bounds__(608, 1)
                         (2 * pr + t) * BM, h);
           ++xl[t];
         }
-        for (int c = 0; c < nE && ok; ++c) {
+        for (int cv = 0; cv < nEv && ok; ++cv) {
+          const int hw = SX ? cv / nE : h;  // head of the weights
+          const int c = SX ? cv % nE : cv;
           {
             const int s = c1 % WS;
             if (!(ok = mbar_wait(&w1_empty[s], ((c1 / WS) & 1) ^ 1, ctx))) break;
             mbar_arrive_expect_tx(&w1_full[s], C::W1_BYTES);
             for (int r = 0; r < ET / 64; ++r)
-              tma_load_3d(sW1 + s * C::W1_BYTES + r * DP * 128, &tm_w1, &w1_full[s], c * ET + 64 * r, 0, h);
+              tma_load_3d(sW1 + s * C::W1_BYTES + r * DP * 128, &tm_w1, &w1_full[s], c * ET + 64 * r, 0, hw);
             ++c1;
           }
           {
@@ -154,7 +164,7 @@ __global__ void __launch_bounds__(608, 1)
             if (!(ok = mbar_wait(&w2_empty[s], ((c2 / WS) & 1) ^ 1, ctx))) break;
             mbar_arrive_expect_tx(&w2_full[s], C::W2_BYTES);
             for (int r = 0; r < DP / 64; ++r)
-              tma_load_3d(sW2 + s * C::W2_BYTES + r * ET * 128, &tm_w2, &w2_full[s], 64 * r, c * ET, h);
+              tma_load_3d(sW2 + s * C::W2_BYTES + r * ET * 128, &tm_w2, &w2_full[s], 64 * r, c * ET, hw);
             ++c2;
           }
         }
@@ -205,9 +215,9 @@ __global__ void __launch_bounds__(608, 1)
 
     for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++it) {
       if (!(ok = warp_wait(&x_full[t], it & 1, ctx))) break;
-      if (!(ok = gemm1(nE == 1))) break;
-      for (int c = 0; c < nE && ok; ++c) {
-        const uint32_t zc = it * nE + c;  // chunk index, for the z/h barrier parities
+      if (!(ok = gemm1(nEv == 1))) break;
+      for (int c = 0; c < nEv && ok; ++c) {
+        const uint32_t zc = it * nEv + c;  // chunk index, for the z/h barrier parities
         const int s2 = c2 % WS;
         if (!(ok = warp_wait(&w2_full[s2], (c2 / WS) & 1, ctx))) break;
         ++c2;
@@ -226,10 +236,10 @@ __global__ void __launch_bounds__(608, 1)
             mma_ts(o_tmem, z_tmem + sl * SW + within / 2, sdesc_add(wd, k * 2048), idesc2, k > 0 ? 1u : acc0);
           }
           mma_commit(&w2_empty[s2]);
-          if (c + 1 == nE) mma_commit(&o_full[t]);
+          if (c + 1 == nEv) mma_commit(&o_full[t]);
         }
         __syncwarp();
-        if (c + 1 < nE && !(ok = gemm1(c + 2 == nE))) break;  // overwrites Z_t after GEMM2 read H_t
+        if (c + 1 < nEv && !(ok = gemm1(c + 2 == nEv))) break;  // overwrites Z_t after GEMM2 read H_t
       }
     }
     if (elect_one()) mma_commit(&done_bar[t]);
@@ -243,10 +253,11 @@ __global__ void __launch_bounds__(608, 1)
     const uint32_t lane_off = uint32_t(q * 32) << 16;
     uint32_t it = 0;
     bool ok = true;
+    const float inv_h = SX ? 1.0f / float(H) : 1.0f;
     for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++it) {
-      const int h = item / nP, pr = item % nP;
-      for (int c = 0; c < nE && ok; ++c) {
-        const uint32_t zc = it * nE + c;
+      const int h = SX ? 0 : item / nP, pr = SX ? item : item % nP;
+      for (int c = 0; c < nEv && ok; ++c) {
+        const uint32_t zc = it * nEv + c;
         for (int t = 0; t < 2; ++t) {
           if (!(ok = mbar_wait(&z_full[t], zc & 1, ctx))) break;
           tc_fence_after();
@@ -276,6 +287,10 @@ __global__ void __launch_bounds__(608, 1)
         } else {
           tmem_ld16_sync(oa, v);
         }
+        if constexpr (SX) {
+#pragma unroll
+          for (int i = 0; i < OW; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * inv_h);
+        }
         plain_pack<T, OW / 2>(v, p);
         tc_fence_before();
         __syncwarp();
@@ -297,18 +312,23 @@ __global__ void __launch_bounds__(608, 1)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
-template <int DP, typename T, int ACT>
-static cudaError_t launch_pair_t(const FwdLaunch& a) {
+template <int DP, typename T, int ACT, bool SX>
+static cudaError_t launch_pair_sx(const FwdLaunch& a) {
   using C = FwdPairCfg<DP>;
-  auto kern = fmlp_fwd_pair_kernel<DP, T, ACT>;
+  auto kern = fmlp_fwd_pair_kernel<DP, T, ACT, SX>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const long long nB = (a.B + kRows - 1) / kRows;
-  const long long items = (long long)a.H * ((nB + 1) / 2);
+  const long long items = (SX ? 1LL : (long long)a.H) * ((nB + 1) / 2);
   const int grid = int(items < a.sm_count ? items : a.sm_count);
   kern<<<grid, C::NUM_THREADS, C::SMEM, a.stream>>>(a.tm_x, a.tm_w1, a.tm_w2, reinterpret_cast<T*>(a.o),
                                                     a.H, a.B, a.D, a.E, a.status);
   return cudaGetLastError();
+}
+
+template <int DP, typename T, int ACT>
+static cudaError_t launch_pair_t(const FwdLaunch& a) {
+  return a.shared_x ? launch_pair_sx<DP, T, ACT, true>(a) : launch_pair_sx<DP, T, ACT, false>(a);
 }
 
 template <int DP, typename T>

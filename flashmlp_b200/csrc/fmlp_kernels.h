@@ -15,6 +15,7 @@ struct FwdLaunch {
   int dp;             // D rounded up to a multiple of 64 (64, 128 or 256)
   int bf16;           // 1 = bfloat16, 0 = float16
   int act;            // fmlp::Act
+  int shared_x;       // 1: X is (B,D) for every head and o is the (B,D) mean over heads
   int grid;           // persistent CTAs (single-tile kernel)
   int sm_count;       // SMs of the device
   uint32_t* status;   // device status word
@@ -37,6 +38,7 @@ struct BwdLaunch {
   int sm_count;
   int H, B, D, E;
   int dp, bf16, act;
+  int shared_x;        // 1: X, dO, dX are (B,D) shared by every head (mean over heads)
   uint32_t* status;
   cudaStream_t stream;
 };

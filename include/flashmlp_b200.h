@@ -65,6 +65,26 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
              int dtype, int act, void* stream);
 
 /*
+ * Shared-input forward: x is ONE (B,D) matrix used by every head and o (B,D) receives the
+ * mean over heads, o = (1/H) * sum_h act(x @ W1[h]) @ W2[h]. This is what the reference's
+ * FlashMLP.forward computes for a 2-D input (flashmlp.py:603-614: x expanded to (H,B,D),
+ * FlashMLPFunction, o.mean(0)) without materialising the H copies of x and of o; the head
+ * sum is accumulated in fp32 and rounded once. Needs H >= 1 and D <= 128.
+ */
+int fmlp_fwd_shared_x(const void* x, const void* w1, const void* w2, void* o, int H, int B, int D,
+                      int E, int dtype, int act, void* stream);
+
+/*
+ * Backward of fmlp_fwd_shared_x: dO (B,D) is the gradient of the head mean, dx (B,D) the
+ * gradient of the shared input (summed over heads, as the expand's backward does), dw1
+ * (H,D,E) and dw2 (H,E,D) per head. Workspace as for fmlp_bwd (fmlp_bwd_workspace_size
+ * with the same H, B, D, E). Needs H >= 1 and D <= 128.
+ */
+int fmlp_bwd_shared_x(const void* x, const void* w1, const void* w2, const void* dO, void* dx,
+                      void* dw1, void* dw2, void* workspace, size_t workspace_bytes, int H, int B,
+                      int D, int E, int dtype, int act, void* stream);
+
+/*
  * The same backward with dW left as unrounded fp32 sums over this call's B rows:
  * dw_f32 holds dW1 laid out (H,D,E) followed by dW2 laid out (H,E,D), 2*H*D*E floats.
  * dx is written as in fmlp_bwd; the workspace rule is fmlp_bwd's. Used by the batch-
