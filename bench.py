@@ -246,14 +246,12 @@ def run_ours(args, rank, world, local_rank):
     h2d = sum(t.numel() * t.element_size() for t in (hx, hw1, hw2, hdo))
     d2h = sum(t.numel() * t.element_size() for t in (ho, hdx, hdw1, hdw2))
 
-    def e2e_step():
-        x_d, w1_d, w2_d = (hx.to(dev, non_blocking=True), hw1.to(dev, non_blocking=True),
-                           hw2.to(dev, non_blocking=True))
-        do_d = hdo.to(dev, non_blocking=True)
-        o_ = F.flashmlp_fwd(x_d, w1_d, w2_d, act)
-        gx, g1, g2 = F.flashmlp_bwd(x_d, w1_d, w2_d, do_d, act)
-        ho.copy_(o_, non_blocking=True); hdx.copy_(gx, non_blocking=True)
-        hdw1.copy_(g1, non_blocking=True); hdw2.copy_(g2, non_blocking=True)
+    from flashmlp_b200.host import HostPipeline
+
+    pipe = HostPipeline(dev, heads_per_group=4)
+
+    def e2e_step():  # host in, host out; head groups pipelined over copy-in/compute/copy-out streams
+        pipe.run(hx, hw1, hw2, hdo, act, out=(ho, hdx, hdw1, hdw2))
 
     e2e_step()
     barrier()
@@ -322,7 +320,9 @@ def run_ours(args, rank, world, local_rank):
         "cpu_baseline": cpu,
         "e2e": {"value": round(fl_step_total * n_e2e / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n_e2e,
-                "path": "flashmlp_fwd/flashmlp_bwd on tensors copied from pinned host memory, outputs copied back"},
+                "path": "flashmlp_b200.host.HostPipeline.run: pinned host X, W1, W2, dO in; O, dX, dW1, dW2 "
+                        "back to pinned host memory; groups of 4 heads pipelined (copy-in / flashmlp_fwd + "
+                        "flashmlp_bwd / copy-out on three streams)"},
         "gpu_launches": launches_per_step * n,
         "clocks": clocks,
         "device_status": status,

@@ -1,0 +1,104 @@
+"""Forward + backward on tensors that live in host memory, with the copies overlapped.
+
+The reference's functions take device tensors (flashmlp.py:428-538); a caller whose data
+sits in host memory first copies X, W1, W2 and dO to the GPU and the results back, and
+those copies (2 x 16-bit x (2*H*B*D + 2*H*D*E) bytes per step) take longer than the
+kernels over PCIe. Heads are independent, so `fwd_bwd_host` cuts the heads into groups
+and pipelines them over three CUDA streams: group g+1 is copied in while group g runs
+through flashmlp_fwd / flashmlp_bwd and group g-1 is copied out. Results are identical to
+flashmlp_fwd / flashmlp_bwd on the whole tensors (the kernels treat heads independently).
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from .api import flashmlp_bwd, flashmlp_fwd
+
+
+def _pinned_like(t: torch.Tensor) -> torch.Tensor:
+    return torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+
+
+class HostPipeline:
+    """Reusable device buffers and streams for `fwd_bwd_host` on one device.
+
+    `heads_per_group` heads move and compute together; `slots` groups are in flight
+    (3: one being copied in, one computing, one being copied out)."""
+
+    def __init__(self, device=None, heads_per_group: int = 4, slots: int = 3):
+        dev = torch.device(device) if device is not None else torch.device("cuda")
+        if dev.type != "cuda":
+            raise RuntimeError("fwd_bwd_host computes on a CUDA device")
+        self.device = dev if dev.index is not None else torch.device("cuda", torch.cuda.current_device())
+        self.hg = max(1, int(heads_per_group))
+        self.slots = max(2, int(slots))
+        self.s_in = torch.cuda.Stream(self.device)
+        self.s_comp = torch.cuda.Stream(self.device)
+        self.s_out = torch.cuda.Stream(self.device)
+        self._key = None
+        self._buf = None
+
+    def _buffers(self, shapes, dtype):
+        key = (shapes, dtype)
+        if self._key != key:
+            xs, w1s, w2s = shapes
+            mk = lambda s: torch.empty(s, dtype=dtype, device=self.device)
+            self._buf = [dict(x=mk(xs), w1=mk(w1s), w2=mk(w2s), do=mk(xs)) for _ in range(self.slots)]
+            self._key = key
+        return self._buf
+
+    def run(self, x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, do: torch.Tensor, activation: str = "",
+            out: Optional[Tuple[torch.Tensor, ...]] = None):
+        """x, do (H, B, D), w1 (H, D, E), w2 (H, E, D) in (preferably pinned) host memory.
+        Returns host tensors (o, dx, dw1, dw2), written into `out` when given."""
+        H, B, D = x.shape
+        E = w1.shape[2]
+        if out is None:
+            out = (_pinned_like(x), _pinned_like(x), _pinned_like(w1), _pinned_like(w2))
+        o_h, dx_h, dw1_h, dw2_h = out
+        hg = min(self.hg, max(H, 1))
+        bufs = self._buffers(((hg, B, D), (hg, D, E), (hg, E, D)), x.dtype)
+        groups = [(h0, min(h0 + hg, H)) for h0 in range(0, H, hg)]
+        ev_in = [torch.cuda.Event() for _ in groups]
+        ev_comp = [torch.cuda.Event() for _ in groups]
+        ev_out = [torch.cuda.Event() for _ in groups]
+        results = [None] * len(groups)
+        # the slots may still be read by the previous call's work, and the caller's stream
+        # may have queued work this call must follow
+        self.s_in.wait_stream(self.s_out)
+        self.s_in.wait_stream(torch.cuda.current_stream(self.device))
+        for g, (a, b) in enumerate(groups):
+            n = b - a
+            slot = bufs[g % self.slots]
+            if g >= self.slots:  # the slot's previous group has been copied out
+                self.s_in.wait_event(ev_out[g - self.slots])
+            with torch.cuda.stream(self.s_in):
+                for k, src in (("x", x), ("w1", w1), ("w2", w2), ("do", do)):
+                    slot[k][:n].copy_(src[a:b], non_blocking=True)
+                ev_in[g].record(self.s_in)
+            self.s_comp.wait_event(ev_in[g])
+            with torch.cuda.stream(self.s_comp):
+                xs, w1s, w2s, dos = (slot[k][:n] for k in ("x", "w1", "w2", "do"))
+                o = flashmlp_fwd(xs, w1s, w2s, activation)
+                dx, dw1, dw2 = flashmlp_bwd(xs, w1s, w2s, dos, activation)
+                results[g] = (o, dx, dw1, dw2)
+                ev_comp[g].record(self.s_comp)
+            self.s_out.wait_event(ev_comp[g])
+            with torch.cuda.stream(self.s_out):
+                for dst, src in zip((o_h, dx_h, dw1_h, dw2_h), results[g]):
+                    dst[a:b].copy_(src, non_blocking=True)
+                    src.record_stream(self.s_out)
+                ev_out[g].record(self.s_out)
+            results[g] = None
+        torch.cuda.current_stream(self.device).wait_stream(self.s_out)
+        return o_h, dx_h, dw1_h, dw2_h
+
+
+def fwd_bwd_host(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, do: torch.Tensor, activation: str = "",
+                 device=None, heads_per_group: int = 4):
+    """One forward + backward of host-resident tensors on `device` (default: the current
+    CUDA device), copies overlapped with the kernels. Returns host (o, dx, dw1, dw2); the
+    host outputs are complete once torch.cuda.current_stream() has synchronised."""
+    return HostPipeline(device, heads_per_group).run(x, w1, w2, do, activation)

@@ -1,6 +1,7 @@
 """Small, profiler-friendly case of the benchmark workload.
 
     python -m flashmlp_b200.profile_case [--heads 4] [--rows 65536] [--act silu] [--iters 3]
+                                         [--shared] [--allreduce]
 
 Runs `iters` forward and `iters` backward launches of the C4 shape restricted to a few
 heads (inputs still larger than L2), so an ncu capture of one launch stays small:
@@ -26,6 +27,10 @@ def main() -> None:
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "f16"])
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--only", choices=["fwd", "bwd", "both"], default="both")
+    ap.add_argument("--shared", action="store_true",
+                    help="shared-input kernels: one (B, D) input for all heads, head mean output")
+    ap.add_argument("--allreduce", action="store_true",
+                    help="instead: fmlp_grad_allreduce_sgd (one rank) and fmlp_sgd_update on 2*H*D*E weights")
     a = ap.parse_args()
     dt = torch.bfloat16 if a.dtype == "bf16" else torch.float16
     H, B, D, E = a.heads, a.rows, a.hidden, a.inter
@@ -34,14 +39,46 @@ def main() -> None:
     w1 = (torch.randn(H, D, E, device="cuda", generator=g) / D ** 0.5).to(dt)
     w2 = (torch.randn(H, E, D, device="cuda", generator=g) / E ** 0.5).to(dt)
     do = torch.randn(H, B, D, device="cuda", generator=g).to(dt)
+    if a.allreduce:
+        _allreduce(a, H, D, E, dt)
+        return
+    if a.shared:
+        x, do = x[0].contiguous(), do[0].contiguous()
+    fwd = api.flashmlp_fwd_shared_x if a.shared else api.flashmlp_fwd
+    bwd = api.flashmlp_bwd_shared_x if a.shared else api.flashmlp_bwd
     for _ in range(a.iters):
         if a.only in ("fwd", "both"):
-            api.flashmlp_fwd(x, w1, w2, a.act)
+            fwd(x, w1, w2, a.act)
         if a.only in ("bwd", "both"):
-            api.flashmlp_bwd(x, w1, w2, do, a.act)
+            bwd(x, w1, w2, do, a.act)
     torch.cuda.synchronize()
     st = _lib.lib().fmlp_device_status(1)
     print(f"profile_case H={H} B={B} D={D} E={E} {a.dtype} {a.act}: status {st}")
+    if st:
+        raise SystemExit(1)
+
+
+def _allreduce(a, H, D, E, dt) -> None:
+    """One-rank fmlp_grad_allreduce_sgd (no barrier; the reduce + update over all n
+    weights) and fmlp_sgd_update, each `iters` times, on n = 2*H*D*E weights."""
+    import ctypes
+
+    n = 2 * H * D * E
+    w = torch.randn(n, device="cuda").to(dt)
+    g = torch.randn(n, device="cuda")
+    flags = torch.zeros(8, dtype=torch.int32, device="cuda")
+    L = _lib.lib()
+    arr = lambda t: (ctypes.c_void_p * 1)(ctypes.c_void_p(t.data_ptr()))
+    code = _lib.FMLP_DTYPE_BF16 if dt == torch.bfloat16 else _lib.FMLP_DTYPE_F16
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for i in range(a.iters):
+        rc = L.fmlp_grad_allreduce_sgd(arr(w), arr(g), arr(flags), 1, 0, n, 1e-4, code, 2 * i + 1, stream)
+        _lib.check(rc, "fmlp_grad_allreduce_sgd")
+        _lib.check(L.fmlp_sgd_update(ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(g.data_ptr()), n, 1e-4, code,
+                                     stream), "fmlp_sgd_update")
+    torch.cuda.synchronize()
+    st = L.fmlp_device_status(1)
+    print(f"profile_case allreduce n={n}: status {st}")
     if st:
         raise SystemExit(1)
 
