@@ -12,6 +12,7 @@ LIB_PATH = Path(__file__).resolve().with_name("libflashmlp_b200.so")
 
 FMLP_DTYPE_F16 = 0
 FMLP_DTYPE_BF16 = 1
+FMLP_DTYPE_F32 = 2
 
 FMLP_ACT_LINEAR = 0
 FMLP_ACT_LEAKY_RELU = 1

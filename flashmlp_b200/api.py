@@ -36,8 +36,10 @@ def _dtype_code(t: torch.Tensor) -> int:
         return _lib.FMLP_DTYPE_BF16
     if t.dtype == torch.float16:
         return _lib.FMLP_DTYPE_F16
+    if t.dtype == torch.float32:  # TF32 tensor-core products, as tl.dot on fp32 tensors
+        return _lib.FMLP_DTYPE_F32
     raise TypeError(
-        f"flashmlp_b200 supports torch.bfloat16 and torch.float16 tensors, got {t.dtype}"
+        f"flashmlp_b200 supports torch.bfloat16, torch.float16 and torch.float32 tensors, got {t.dtype}"
     )
 
 
@@ -267,10 +269,11 @@ class FlashMLP(torch.nn.Module):
 
     Parameters `w1` (H, D, E) and `w2` (H, E, D) are initialised like the reference,
     randn / sqrt(E) and randn / sqrt(D), so state dicts interchange. A 2-D input (B, D) is
-    broadcast to every head and the output is averaged over heads; for D <= 128 this runs
-    on the shared-input kernels (no (H, B, D) copies of x, dO or dX; the head mean is
-    accumulated in fp32), for larger D on the per-head kernels with the expanded input,
-    as in the reference (flashmlp.py:603-614).
+    broadcast to every head and the output is averaged over heads; for 16-bit inputs with
+    D <= 128 this runs on the shared-input kernels (no (H, B, D) copies of x, dO or dX; the
+    head mean is accumulated in fp32), otherwise on the per-head kernels with the expanded
+    input, as in the reference (flashmlp.py:603-614). float32 parameters run on the TF32
+    kernels (D <= 128).
     """
 
     def __init__(self, num_heads: int, hidden_dim: int, intermediate_dim: int,
@@ -291,7 +294,7 @@ class FlashMLP(torch.nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         squeeze_output = x.dim() == 2
-        if squeeze_output and x.shape[-1] <= 128 and self.num_heads > 0:
+        if squeeze_output and x.shape[-1] <= 128 and self.num_heads > 0 and x.dtype != torch.float32:
             return FlashMLPSharedInputFunction.apply(x, self.w1, self.w2, self.activation)
         if squeeze_output:
             x = x.unsqueeze(0).expand(self.num_heads, -1, -1)

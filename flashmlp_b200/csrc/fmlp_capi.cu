@@ -58,17 +58,20 @@ int device_info(DeviceInfo** out) {
   return FMLP_OK;
 }
 
-// 3-D tiled map over a contiguous (d2, d1, d0) row-major tensor of 16-bit elements,
-// 128-byte swizzle, zero fill out of bounds.
-int encode3d(CUtensorMap* m, const void* ptr, int bf16, uint64_t d0, uint64_t d1, uint64_t d2,
-             uint32_t b0, uint32_t b1) {
+// 3-D tiled map over a contiguous (d2, d1, d0) row-major tensor of `dtype` elements
+// (FMLP_DTYPE_*), 128-byte swizzle, zero fill out of bounds.
+int encode3d(CUtensorMap* m, const void* ptr, int dtype, uint64_t d0, uint64_t d1, uint64_t d2,
+             uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  const uint64_t esz = dtype == FMLP_DTYPE_F32 ? 4 : 2;
+  const CUtensorMapDataType dt = dtype == FMLP_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == FMLP_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   cuuint64_t dims[3] = {d0, d1, d2};
-  cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+  cuuint64_t strides[2] = {d0 * esz, d0 * d1 * esz};
   cuuint32_t box[3] = {b0, b1, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        3, const_cast<void*>(ptr), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  CUresult r = g_encode(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? FMLP_OK : FMLP_ERR_TMA;
 }
@@ -77,7 +80,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int check_common(int H, int B, int D, int E, int dtype) {
   if (H < 0 || B < 0 || D < 0 || E < 0) return FMLP_ERR_INVALID_SHAPE;
-  if (dtype != FMLP_DTYPE_F16 && dtype != FMLP_DTYPE_BF16) return FMLP_ERR_UNSUPPORTED_DTYPE;
+  if (dtype != FMLP_DTYPE_F16 && dtype != FMLP_DTYPE_BF16 && dtype != FMLP_DTYPE_F32)
+    return FMLP_ERR_UNSUPPORTED_DTYPE;
   const long long hb = (long long)H * B, hd = (long long)H * D;
   if (hb * D >= (1LL << 40) || hd * E >= (1LL << 40)) return FMLP_ERR_INVALID_SHAPE;
   if (B > (1 << 30) || E > (1 << 30)) return FMLP_ERR_INVALID_SHAPE;
@@ -85,6 +89,8 @@ int check_common(int H, int B, int D, int E, int dtype) {
 }
 
 int round_dp(int D) { return D <= 64 ? 64 : (D <= 128 ? 128 : 256); }
+
+size_t elem_bytes(int dtype) { return dtype == FMLP_DTYPE_F32 ? 4 : 2; }
 
 int cuda_rc(cudaError_t e) { return e == cudaSuccess ? FMLP_OK : FMLP_ERR_CUDA; }
 
@@ -124,9 +130,11 @@ const char* fmlp_error_string(int code) {
   switch (code) {
     case FMLP_OK: return "ok";
     case FMLP_ERR_INVALID_SHAPE: return "invalid shape (negative size or too large)";
-    case FMLP_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype (only float16 and bfloat16)";
+    case FMLP_ERR_UNSUPPORTED_DTYPE:
+      return "unsupported dtype (float16, bfloat16; float32 only for the per-head fmlp_fwd/fmlp_bwd)";
     case FMLP_ERR_UNSUPPORTED_D:
-      return "unsupported hidden dim D (needs D % 16 == 0 and D <= 256; D <= 128 for the shared-input entry points)";
+      return "unsupported hidden dim D (needs D % 16 == 0 and D <= 256; D <= 128 for float32 and for the "
+             "shared-input entry points)";
     case FMLP_ERR_UNSUPPORTED_E: return "unsupported intermediate dim E (needs E % 8 == 0)";
     case FMLP_ERR_MISALIGNED: return "tensor data pointer is not 16-byte aligned";
     case FMLP_ERR_CUDA: return "CUDA runtime error";
@@ -151,7 +159,9 @@ int fwd_impl(const void* x, const void* w1, const void* w2, void* o, int H, int 
              int act, int shared_x, void* stream) {
   int rc = check_common(H, B, D, E, dtype);
   if (rc) return rc;
-  if (D % 16 != 0 || D > (shared_x ? 128 : 256)) return FMLP_ERR_UNSUPPORTED_D;
+  const bool f32 = dtype == FMLP_DTYPE_F32;
+  if (f32 && shared_x) return FMLP_ERR_UNSUPPORTED_DTYPE;
+  if (D % 16 != 0 || D > (shared_x || f32 ? 128 : 256)) return FMLP_ERR_UNSUPPORTED_D;
   if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
   if (shared_x && H == 0) return FMLP_ERR_INVALID_SHAPE;  // no mean over zero heads
   DeviceInfo* dev = nullptr;
@@ -159,15 +169,19 @@ int fwd_impl(const void* x, const void* w1, const void* w2, void* o, int H, int 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t o_elems = size_t(shared_x ? 1 : H) * B * D;
   if (o_elems == 0) return FMLP_OK;
-  if (E == 0) return cuda_rc(cudaMemsetAsync(o, 0, o_elems * 2, st));
+  if (E == 0) return cuda_rc(cudaMemsetAsync(o, 0, o_elems * elem_bytes(dtype), st));
   if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(o)) return FMLP_ERR_MISALIGNED;
   FwdLaunch a{};
   a.dp = round_dp(D);
-  const int et = fwd_et(a.dp);
+  const int et = f32 ? 64 : fwd_et(a.dp);
+  const uint32_t inner = f32 ? 32 : 64;  // elements per 128-byte swizzled row
+  // fp32: the weight chunks are read MN-major only, which needs the 32-byte-atom swizzle
+  const CUtensorMapSwizzle wswz = f32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  if ((rc = encode3d(&a.tm_x, x, dtype, D, B, shared_x ? 1 : H, inner, kRows))) return rc;
+  if ((rc = encode3d(&a.tm_w1, w1, dtype, E, D, H, inner, a.dp, wswz))) return rc;
+  if ((rc = encode3d(&a.tm_w2, w2, dtype, D, E, H, inner, et, wswz))) return rc;
   const int bf = dtype == FMLP_DTYPE_BF16;
-  if ((rc = encode3d(&a.tm_x, x, bf, D, B, shared_x ? 1 : H, 64, kRows))) return rc;
-  if ((rc = encode3d(&a.tm_w1, w1, bf, E, D, H, 64, a.dp))) return rc;
-  if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, et))) return rc;
+  a.f32 = f32;
   a.o = o;
   a.H = H, a.B = B, a.D = D, a.E = E;
   a.bf16 = bf;
@@ -178,7 +192,7 @@ int fwd_impl(const void* x, const void* w1, const void* w2, void* o, int H, int 
   a.sm_count = dev->sm_count;
   a.status = dev->status;
   a.stream = st;
-  return cuda_rc(launch_fwd(a));
+  return cuda_rc(f32 ? launch_fwd_tf32(a) : launch_fwd(a));
 }
 
 }  // namespace
@@ -197,6 +211,7 @@ int fmlp_fwd_shared_x(const void* x, const void* w1, const void* w2, void* o, in
 
 size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {
   if (check_common(H, B, D, E, dtype) || D % 16 != 0 || D > 256 || E % 8 != 0) return 0;
+  if (dtype == FMLP_DTYPE_F32) return 0;  // the fp32 backward does not split its dW programs
   DeviceInfo* dev = nullptr;
   if (device_info(&dev)) return 0;
   return bwd_workspace_bytes(H, B, D, E, dev->sm_count);
@@ -213,21 +228,24 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
              int shared_x, void* stream) {
   int rc = check_common(H, B, D, E, dtype);
   if (rc) return rc;
-  if (D % 16 != 0 || D > (shared_x ? 128 : 256)) return FMLP_ERR_UNSUPPORTED_D;
+  const bool f32 = dtype == FMLP_DTYPE_F32;
+  if (f32 && shared_x) return FMLP_ERR_UNSUPPORTED_DTYPE;
+  if (D % 16 != 0 || D > (shared_x || f32 ? 128 : 256)) return FMLP_ERR_UNSUPPORTED_D;
   if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
   if (shared_x && H == 0) return FMLP_ERR_INVALID_SHAPE;
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
-  const size_t ws_need = bwd_workspace_bytes(H, B, D, E, dev->sm_count);
+  const size_t ws_need = f32 ? 0 : bwd_workspace_bytes(H, B, D, E, dev->sm_count);
   if (workspace_bytes < ws_need || (ws_need && (workspace == nullptr || !aligned16(workspace))))
     return FMLP_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (H == 0 || D == 0) return FMLP_OK;
-  if (E == 0) return cuda_rc(cudaMemsetAsync(dx, 0, size_t(shared_x ? 1 : H) * B * D * 2, st));
+  const size_t esz = elem_bytes(dtype);
+  if (E == 0) return cuda_rc(cudaMemsetAsync(dx, 0, size_t(shared_x ? 1 : H) * B * D * esz, st));
   if (B == 0) {
     if (dwf) return cuda_rc(cudaMemsetAsync(dwf, 0, size_t(2) * H * D * E * sizeof(float), st));
-    if ((rc = cuda_rc(cudaMemsetAsync(dw1, 0, size_t(H) * D * E * 2, st)))) return rc;
-    return cuda_rc(cudaMemsetAsync(dw2, 0, size_t(H) * E * D * 2, st));
+    if ((rc = cuda_rc(cudaMemsetAsync(dw1, 0, size_t(H) * D * E * esz, st)))) return rc;
+    return cuda_rc(cudaMemsetAsync(dw2, 0, size_t(H) * E * D * esz, st));
   }
   if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(dO) || !aligned16(dx))
     return FMLP_ERR_MISALIGNED;
@@ -235,12 +253,28 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
   BwdLaunch a{};
   a.dp = round_dp(D);
   const int bf = dtype == FMLP_DTYPE_BF16;
-  const int rows = a.dp == 256 ? 64 : kRows;  // B rows and W2 E rows per TMA box
-  const int hx = shared_x ? 1 : H;  // heads of X / dO
-  if ((rc = encode3d(&a.tm_x, x, bf, D, B, hx, 64, rows))) return rc;
-  if ((rc = encode3d(&a.tm_do, dO, bf, D, B, hx, 64, rows))) return rc;
-  if ((rc = encode3d(&a.tm_w1, w1, bf, E, D, H, 64, a.dp))) return rc;
-  if ((rc = encode3d(&a.tm_w2, w2, bf, D, E, H, 64, a.dp == 256 ? 64 : kBwdEt))) return rc;
+  // B rows and W2 E rows per TMA box: 128 for 16-bit D <= 128; 64 for D = 256 and fp32
+  const int rows = (a.dp == 256 || f32) ? 64 : kRows;
+  const uint32_t inner = f32 ? 32 : 64;  // elements per 128-byte swizzled row
+  const int hx = shared_x ? 1 : H;       // heads of X / dO
+  Tf32BwdMaps tm32;
+  if (f32) {  // 32-row boxes; tiles read MN-major get a second map with 32-byte atoms
+    const CUtensorMapSwizzle mn = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    if ((rc = encode3d(&tm32.x_k, x, dtype, D, B, H, 32, 32))) return rc;
+    if ((rc = encode3d(&tm32.x_mn, x, dtype, D, B, H, 32, 32, mn))) return rc;
+    if ((rc = encode3d(&tm32.do_k, dO, dtype, D, B, H, 32, 32))) return rc;
+    if ((rc = encode3d(&tm32.do_mn, dO, dtype, D, B, H, 32, 32, mn))) return rc;
+    if ((rc = encode3d(&tm32.w1_k, w1, dtype, E, D, H, 32, a.dp))) return rc;
+    if ((rc = encode3d(&tm32.w1_mn, w1, dtype, E, D, H, 32, a.dp, mn))) return rc;
+    if ((rc = encode3d(&tm32.w2_k, w2, dtype, D, E, H, 32, 32))) return rc;
+    a.tf32_maps = &tm32;
+  } else {
+    if ((rc = encode3d(&a.tm_x, x, dtype, D, B, hx, inner, rows))) return rc;
+    if ((rc = encode3d(&a.tm_do, dO, dtype, D, B, hx, inner, rows))) return rc;
+    if ((rc = encode3d(&a.tm_w1, w1, dtype, E, D, H, inner, a.dp))) return rc;
+    if ((rc = encode3d(&a.tm_w2, w2, dtype, D, E, H, inner, rows))) return rc;
+  }
+  a.f32 = f32;
   a.x = x, a.w1 = w1;
   a.dx = dx, a.dw1 = dw1, a.dw2 = dw2;
   a.dw_f32 = dwf;
@@ -253,7 +287,7 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
   a.shared_x = shared_x;
   a.status = dev->status;
   a.stream = st;
-  return cuda_rc(launch_bwd(a));
+  return cuda_rc(f32 ? launch_bwd_tf32(a) : launch_bwd(a));
 }
 
 }  // namespace

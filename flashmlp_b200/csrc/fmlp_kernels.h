@@ -13,13 +13,22 @@ struct FwdLaunch {
   void* o;            // O  (H,B,D)  row-major, written directly
   int H, B, D, E;
   int dp;             // D rounded up to a multiple of 64 (64, 128 or 256)
-  int bf16;           // 1 = bfloat16, 0 = float16
+  int bf16;           // 1 = bfloat16, 0 = float16 (fp32 inputs: f32 = 1)
+  int f32;            // 1 = float32 inputs and outputs (TF32 products)
   int act;            // fmlp::Act
   int shared_x;       // 1: X is (B,D) for every head and o is the (B,D) mean over heads
   int grid;           // persistent CTAs (single-tile kernel)
   int sm_count;       // SMs of the device
   uint32_t* status;   // device status word
   cudaStream_t stream;
+};
+
+// Tensor maps of the fp32 (TF32) backward: *_k with the 128-byte swizzle (tiles read
+// K-major), *_mn with the 128-byte swizzle of 32-byte atoms (tiles read MN-major, the
+// only MN-major layout of TF32 operands). Boxes {32 elements, rows}: X, dO and W2 32 rows,
+// W1 DP rows.
+struct Tf32BwdMaps {
+  CUtensorMap x_k, x_mn, do_k, do_mn, w1_k, w1_mn, w2_k;
 };
 
 struct BwdLaunch {
@@ -34,10 +43,12 @@ struct BwdLaunch {
   void* dw2;
   float* part;         // fp32 dW partial sums of split dW programs (splits > 1), else null
   float* dw_f32;       // if set: dW1 (H,D,E) then dW2 (H,E,D) as unrounded fp32, not dw1/dw2
+  const Tf32BwdMaps* tf32_maps;  // fp32 inputs only
   int splits;          // dW programs per (head, E chunk); 1 = no split (DP <= 128 only)
   int sm_count;
   int H, B, D, E;
   int dp, bf16, act;
+  int f32;             // 1 = float32 inputs and outputs (TF32 products)
   int shared_x;        // 1: X, dO, dX are (B,D) shared by every head (mean over heads)
   uint32_t* status;
   cudaStream_t stream;
@@ -55,6 +66,8 @@ cudaError_t launch_fwd(const FwdLaunch& a);       // picks the kernel for a.dp
 cudaError_t launch_fwd_pair(const FwdLaunch& a);  // two row tiles per CTA, D <= 128
 cudaError_t launch_bwd(const BwdLaunch& a);     // picks the kernel for a.dp
 cudaError_t launch_bwd256(const BwdLaunch& a);  // 128 < D <= 256
+cudaError_t launch_fwd_tf32(const FwdLaunch& a);  // fp32 inputs, TF32 products, D <= 128
+cudaError_t launch_bwd_tf32(const BwdLaunch& a);
 int bwd256_smem_bytes();
 // SM count and device status word of the current device (fails if it is not an sm_100).
 int current_device_status(int* sm_count, uint32_t** status);

@@ -174,6 +174,28 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       : "memory");
 }
 
+// TF32 forms (kind::tf32): fp32 operands used at TF32 precision (10-bit mantissa),
+// fp32 accumulation; one K-step is 8 elements (32 bytes of a 128-byte row, or 8 TMEM
+// columns for an A operand in TMEM).
+__device__ __forceinline__ void mma_ss_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_tf32(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on `bar` when every tcgen05 async op issued so far by this thread is done.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
@@ -295,6 +317,13 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(bool bf16, int M, int N, b
          ((uint32_t(N) >> 3) << 17) | ((uint32_t(M) >> 4) << 24);
 }
 
+// Instruction descriptor for tcgen05.mma kind::tf32 (A and B format 2 = TF32), fp32
+// accumulation; fields as in make_idesc_f16.
+__host__ __device__ constexpr uint32_t make_idesc_tf32(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t(N) >> 3) << 17) | ((uint32_t(M) >> 4) << 24);
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100 version bit.
 //   [0,14) start>>4, [16,30) LBO>>4, [32,46) SBO>>4, bit 46 version, [61,64) layout type.
 // Tiles are laid out the way TMA writes a box whose inner extent is 128 bytes with
@@ -312,6 +341,31 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_
   d |= uint64_t(1) << 46;
   d |= uint64_t(2) << 61;
   return d;
+}
+
+// Shared-memory matrix descriptor for an MN-major 32-bit (TF32) operand: layout type 1
+// (128-byte swizzle span with 32-byte atoms, what TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B), the only MN-major layout TF32 operands support.
+// Rows of 128 bytes (32 MN elements); atoms of 4 K-rows, SBO = 512 bytes between them;
+// LBO = byte distance to the next group of 32 MN elements. A K-step of 8 rows is +1024 B.
+__device__ __forceinline__ uint64_t make_sdesc_mn32(uint32_t smem_addr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= uint64_t((smem_addr >> 4) & 0x3FFFu);
+  d |= uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= uint64_t((512u >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(1) << 61;
+  return d;
+}
+
+// Warp-wide 8-column TMEM load (32 lanes x 8 consecutive 32-bit columns), waited.
+__device__ __forceinline__ void tmem_ld8_sync(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
 }
 
 // The same descriptor with its start address moved by `bytes` (a multiple of 16; shared
@@ -358,6 +412,12 @@ struct Pack<__half> {
   __device__ __forceinline__ static float hi(uint32_t p) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(p >> 16)));
   }
+};
+
+template <>
+struct Pack<float> {  // fp32 inputs (TF32 products): nothing is rounded between the products
+  static constexpr bool kBF16 = false;
+  __device__ __forceinline__ static float round(float x) { return x; }
 };
 
 // tanh on the SFU (one MUFU op), max relative error about 2^-11.

@@ -23,6 +23,9 @@ extern "C" {
 /* dtype codes */
 #define FMLP_DTYPE_F16 0
 #define FMLP_DTYPE_BF16 1
+#define FMLP_DTYPE_F32 2 /* fp32 in and out, TF32 tensor-core products (the reference's fp32
+                            path: tl.dot on fp32 tensors); fmlp_fwd / fmlp_bwd /
+                            fmlp_bwd_dw_f32 with D <= 128 */
 
 /* activation codes; the reference treats any unknown activation string as linear
  * (flashmlp.py:146-147, :682-683) and so does the Python layer of this library. */
@@ -34,8 +37,8 @@ extern "C" {
 /* error codes */
 #define FMLP_OK 0
 #define FMLP_ERR_INVALID_SHAPE 1    /* negative size or size overflow                  */
-#define FMLP_ERR_UNSUPPORTED_DTYPE 2 /* only fp16 and bf16                             */
-#define FMLP_ERR_UNSUPPORTED_D 3    /* D % 16 != 0, or D > 256                          */
+#define FMLP_ERR_UNSUPPORTED_DTYPE 2 /* fp16, bf16; fp32 only where noted           */
+#define FMLP_ERR_UNSUPPORTED_D 3    /* D % 16 != 0, or D > 256 (> 128: fp32, shared x)  */
 #define FMLP_ERR_UNSUPPORTED_E 4    /* E % 8 != 0 (row stride of W1 must be 16 bytes)  */
 #define FMLP_ERR_MISALIGNED 5       /* a pointer is not 16-byte aligned                */
 #define FMLP_ERR_CUDA 6             /* CUDA runtime / launch error                     */

@@ -9,7 +9,7 @@ if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-GOLDEN_CASES = ["f16_main", "f16_tail", "f16_c1", "bf16_main", "bf16_c3"]
+GOLDEN_CASES = ["f16_main", "f16_tail", "f16_c1", "bf16_main", "bf16_c3", "f32_main"]
 
 
 def pytest_configure(config):
@@ -28,7 +28,7 @@ def load_golden(name: str) -> dict:
            "acts": [str(a) for a in z["acts"]]}
     for k in ("x", "w1", "w2", "do"):
         a = z[k]
-        out[k] = a.astype(np.float32) if dtype == "f16" else orc.bf16_from_bits(a)
+        out[k] = a.astype(np.float32) if dtype in ("f16", "f32") else orc.bf16_from_bits(a)
     for k in z.files:
         if k.startswith(("torch_", "triton_")):
             out[k] = z[k].astype(np.float32)

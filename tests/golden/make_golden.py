@@ -15,8 +15,12 @@ For every case the reference's own code produces the expected outputs:
     The interpreter cannot run bfloat16 and the reference's kernels require a power-of-two
     D (and its forward needs B and E to be multiples of its tiles: the B/E tails are
     handled wrongly there), so those cases carry only the "torch_*" outputs.
+    The float32 case runs the Triton kernels on float32 tensors: the interpreter evaluates
+    tl.dot in full fp32 (on a GPU it would use TF32).
 Inputs are seeded (numpy default_rng) with X ~ N(0,1), W1 ~ N(0,1/D), W2 ~ N(0,1/E),
-dO ~ N(0,1) and rounded to the 16-bit dtype.
+dO ~ N(0,1) and rounded to the 16-bit dtype (float32 inputs are not rounded).
+
+    python tests/golden/make_golden.py REF_DIR [CASE ...]   # only the named cases
 """
 from __future__ import annotations
 
@@ -43,21 +47,29 @@ CASES = [
     ("f16_c1", (2, 128, 64, 256), "f16", ["silu"], (64, 64), (64, 64)),
     ("bf16_main", (2, 64, 64, 128), "bf16", ACTS, None, None),
     ("bf16_c3", (1, 200, 96, 200), "bf16", ["", "sigmoid"], None, None),
+    ("f32_main", (2, 64, 64, 128), "f32", ACTS, (32, 32), (32, 32)),
 ]
 
 
 def _store_inputs(out: dict, arrs, dtype: str) -> None:
     for k, a in zip(("x", "w1", "w2", "do"), arrs):
-        out[k] = a.astype(np.float16) if dtype == "f16" else orc.bf16_bits(a)
+        if dtype == "f16":
+            out[k] = a.astype(np.float16)
+        elif dtype == "f32":
+            out[k] = a.astype(np.float32)
+        else:
+            out[k] = orc.bf16_bits(a)
 
 
-def main(ref_dir: str) -> None:
+def main(ref_dir: str, only=()) -> None:
     sys.path.insert(0, ref_dir)
     import torch
     import triton
     import flashmlp as ref  # the reference module (flashmlp.py)
 
     for seed, (name, (H, B, D, E), dtype, acts, ftiles, btiles) in enumerate(CASES):
+        if only and name not in only:
+            continue
         x, w1, w2, do = orc.make_inputs(H, B, D, E, dtype, seed=100 + seed)
         out = {"shape": np.array([H, B, D, E]), "dtype": np.array(dtype), "acts": np.array(acts)}
         _store_inputs(out, (x, w1, w2, do), dtype)
@@ -70,9 +82,10 @@ def main(ref_dir: str) -> None:
             out[f"torch_dx_{tag}"] = dx.numpy()
             out[f"torch_dw1_{tag}"] = dw1.numpy()
             out[f"torch_dw2_{tag}"] = dw2.numpy()
-            if dtype != "f16":
+            if dtype == "bf16":
                 continue
-            hx, hw1, hw2, hdo = (t.half() for t in (tx, tw1, tw2, tdo))
+            cast = (lambda t: t.half()) if dtype == "f16" else (lambda t: t.float())
+            hx, hw1, hw2, hdo = (cast(t) for t in (tx, tw1, tw2, tdo))
             xr, w1r, w2r = hx.reshape(H * B, D), hw1.reshape(D * H, E), hw2.reshape(E * H, D)
             if ftiles is not None:
                 bb, be = ftiles
@@ -104,6 +117,6 @@ def main(ref_dir: str) -> None:
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        raise SystemExit("usage: make_golden.py REF_DIR")
-    main(sys.argv[1])
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: make_golden.py REF_DIR [CASE ...]")
+    main(sys.argv[1], tuple(sys.argv[2:]))

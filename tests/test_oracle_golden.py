@@ -9,7 +9,7 @@
 import numpy as np
 import pytest
 
-from conftest import GOLDEN_CASES
+from conftest import load_golden, GOLDEN_CASES
 from oracle import flashmlp_oracle as orc
 
 
@@ -61,6 +61,19 @@ def test_oracle_matches_reference_triton_kernels(golden, case):
             _assert_kernel_match(dw2, g[f"triton_dw2_{tag}"], f"{case}/{tag}/dw2")
             checked += 1
     assert checked > 0
+
+
+def test_oracle_matches_reference_triton_kernels_fp32():
+    # float32 case: the reference's Triton kernels under the interpreter evaluate tl.dot in
+    # full fp32 and round nothing between the products; so does the oracle's "f32" path
+    g = load_golden("f32_main")
+    for act in g["acts"]:
+        tag = act or "linear"
+        o = orc.fwd_kernel(g["x"], g["w1"], g["w2"], act, "f32")
+        np.testing.assert_allclose(o, g[f"triton_o_{tag}"], rtol=1e-5, atol=1e-5, err_msg=f"{tag}/o")
+        got = orc.bwd_kernel(g["x"], g["w1"], g["w2"], g["do"], act, "f32")
+        for name, a in zip(("dx", "dw1", "dw2"), got):
+            np.testing.assert_allclose(a, g[f"triton_{name}_{tag}"], rtol=1e-5, atol=1e-5, err_msg=f"{tag}/{name}")
 
 
 def test_bf16_rounding_is_round_to_nearest_even():
