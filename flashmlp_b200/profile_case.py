@@ -24,7 +24,7 @@ def main() -> None:
     ap.add_argument("--hidden", type=int, default=128)
     ap.add_argument("--inter", type=int, default=2048)
     ap.add_argument("--act", default="silu")
-    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f16"])
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f16", "f32"])
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--only", choices=["fwd", "bwd", "both"], default="both")
     ap.add_argument("--shared", action="store_true",
@@ -32,7 +32,7 @@ def main() -> None:
     ap.add_argument("--allreduce", action="store_true",
                     help="instead: fmlp_grad_allreduce_sgd (one rank) and fmlp_sgd_update on 2*H*D*E weights")
     a = ap.parse_args()
-    dt = torch.bfloat16 if a.dtype == "bf16" else torch.float16
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[a.dtype]
     H, B, D, E = a.heads, a.rows, a.hidden, a.inter
     g = torch.Generator(device="cuda").manual_seed(0)
     x = torch.randn(H, B, D, device="cuda", generator=g).to(dt)
