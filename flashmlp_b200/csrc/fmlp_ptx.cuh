@@ -283,6 +283,19 @@ __device__ __forceinline__ void tmem_wait_ld_dep(uint32_t (&r)[16]) {
                : "memory");
 }
 
+// Waits for every outstanding tcgen05.ld of this thread; both register sets of two
+// asynchronous loads are in/out operands, so no use of either can move above the wait.
+__device__ __forceinline__ void tmem_wait_ld_dep2(uint32_t (&r)[16], uint32_t (&s)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
+                 "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(s[0]), "+r"(s[1]), "+r"(s[2]), "+r"(s[3]),
+                 "+r"(s[4]), "+r"(s[5]), "+r"(s[6]), "+r"(s[7]), "+r"(s[8]), "+r"(s[9]), "+r"(s[10]),
+                 "+r"(s[11]), "+r"(s[12]), "+r"(s[13]), "+r"(s[14]), "+r"(s[15])
+               :
+               : "memory");
+}
+
 // Warp-wide: 8 registers per thread -> 32 lanes x 8 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile(
