@@ -248,7 +248,8 @@ def run_ours(args, rank, world, local_rank):
 
     from flashmlp_b200.host import HostPipeline
 
-    pipe = HostPipeline(dev, heads_per_group=4)
+    hpg = max(1, Hl // 8)  # about 8 groups in flight: 4 heads at N=1, 1 head at N=8
+    pipe = HostPipeline(dev, heads_per_group=hpg)
 
     def e2e_step():  # host in, host out; head groups pipelined over copy-in/compute/copy-out streams
         pipe.run(hx, hw1, hw2, hdo, act, out=(ho, hdx, hdw1, hdw2))
@@ -321,8 +322,8 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": round(fl_step_total * n_e2e / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n_e2e,
                 "path": "flashmlp_b200.host.HostPipeline.run: pinned host X, W1, W2, dO in; O, dX, dW1, dW2 "
-                        "back to pinned host memory; groups of 4 heads pipelined (copy-in / flashmlp_fwd + "
-                        "flashmlp_bwd / copy-out on three streams)"},
+                        f"back to pinned host memory; groups of {hpg} head(s) pipelined (copy-in / flashmlp_fwd "
+                        "+ flashmlp_bwd / copy-out on three streams)"},
         "gpu_launches": launches_per_step * n,
         "clocks": clocks,
         "device_status": status,
