@@ -234,9 +234,11 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms, fwd_avg, bwd_avg = (float(v) for v in t.tolist())
     status = F._lib.lib().fmlp_device_status(1)
-    # fmlp_fwd_*_kernel + fmlp_bwd_kernel, + fmlp_dw_reduce_kernel when the dW programs are
-    # split (the backward then needs a workspace)
-    launches_per_step = 2 + (1 if F._lib.lib().fmlp_bwd_workspace_size(Hl, B, D, E, 1) else 0)
+    # fmlp_fwd_pair_kernel + the backward's launches: fmlp_bwd_kernel, fmlp_dx_gemm_kernel in
+    # the dZ-store mode, fmlp_dw_reduce_kernel when the dW programs are split
+    bwd_ws = int(F._lib.lib().fmlp_bwd_workspace_size(Hl, B, D, E, 1))
+    bwd_mode, bwd_splits, bwd_launches = F._lib.bwd_plan(Hl, B, D, E, 1, bwd_ws)
+    launches_per_step = 1 + bwd_launches
 
     # ---- e2e through the public API with host buffers (pinned), copies inside the timed region
     n_e2e = max(1, min(n, 5))
@@ -283,13 +285,17 @@ def run_ours(args, rank, world, local_rank):
     fwd_fl = 4.0 * Hl * B * D * E
     bwd_tf = bwd_fl / (bwd_avg / 1e3) / 1e12
     fwd_tf = fwd_fl / (fwd_avg / 1e3) / 1e12
+    # DRAM bytes of the backward's launches (ncu, per head, scaled to this launch's heads)
     traffic = None
     tp = ROOT / "profiles" / "roofline_traffic.json"
     if tp.exists():
         try:
-            traffic = json.loads(tp.read_text())["fmlp_bwd_kernel"]["bytes_per_launch_per_head"] * Hl
+            key = "fmlp_bwd_dz_store" if bwd_mode == 1 else "fmlp_bwd_kernel"
+            traffic = json.loads(tp.read_text())[key]["bytes_per_launch_per_head"] * Hl
         except Exception:
             traffic = None
+    bwd_kernels = ("fmlp_bwd_kernel (dW programs, storing dZ^T) + fmlp_dx_gemm_kernel" if bwd_mode == 1
+                   else "fmlp_bwd_kernel") + (" + fmlp_dw_reduce_kernel" if bwd_splits > 1 else "")
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -307,17 +313,20 @@ def run_ours(args, rank, world, local_rank):
                    "heads_per_gpu": Hl, "parallelism": f"head-sharded x{world} (no communication)",
                    "l2": "inputs larger than L2 every step (X and dO are 2x64-512 MiB per GPU); no flush"},
         "roofline": {
-            "bound": "tensor", "kernel": "fmlp_bwd_kernel",
+            "bound": "tensor", "kernel": "fmlp_bwd: " + bwd_kernels,
             "achieved": round(bwd_tf, 2), "peak": peak_sus, "unit": "TFLOP/s",
             "frac": round(bwd_tf / peak_sus, 4), "traffic": traffic,
             "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step loop)",
             "algorithmic_flops_per_launch": bwd_fl,
+            "bwd_mode": "dz-store" if bwd_mode == 1 else "recompute", "bwd_dw_splits": bwd_splits,
         },
         "fwd_ms": round(fwd_avg, 4), "bwd_ms": round(bwd_avg, 4),
         "fwd_tflops": round(fwd_tf, 2), "bwd_tflops": round(bwd_tf, 2),
         "frac_of_measured_burst": round(value / world / peak_burst, 4),
         "frac_of_spec_2250": round(value / world / SPEC_BF16_TFLOPS, 4),
-        "executed_tensor_flops_per_step": 18.0 * H * B * D * E,
+        # tensor FLOPs the kernels execute: forward 4, backward 8 for the dW programs (Z^T,
+        # dH^T, dW1, dW2) plus 2 (dX GEMM) in the dZ-store mode or 6 (dX programs) otherwise
+        "executed_tensor_flops_per_step": (14.0 if bwd_mode == 1 else 18.0) * H * B * D * E,
         "cpu_baseline": cpu,
         "e2e": {"value": round(fl_step_total * n_e2e / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n_e2e,

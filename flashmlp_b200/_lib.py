@@ -29,6 +29,7 @@ FMLP_IPC_HANDLE_BYTES = 64
 
 # Every symbol the header declares, with (restype, argtypes).
 _c_int, _c_vp, _c_sz = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
+_c_ip = ctypes.POINTER(ctypes.c_int)
 SIGNATURES = {
     "fmlp_fwd": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp]),
     "fmlp_bwd": (
@@ -37,6 +38,8 @@ SIGNATURES = {
          _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp],
     ),
     "fmlp_bwd_workspace_size": (_c_sz, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "fmlp_bwd_workspace_size_min": (_c_sz, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "fmlp_bwd_plan": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_sz, _c_ip, _c_ip, _c_ip]),
     "fmlp_bwd_noalloc": (
         _c_int,
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
@@ -104,3 +107,12 @@ def error_string(code: int) -> str:
 def check(code: int, where: str) -> None:
     if code != FMLP_OK:
         raise FlashMLPError(code, where)
+
+
+def bwd_plan(H: int, B: int, D: int, E: int, dtype_code: int, workspace_bytes: int):
+    """(mode, splits, launches) that fmlp_bwd runs for this shape and workspace size on the
+    current device: mode 1 = dZ-store, 0 = recompute (fmlp_bwd_plan)."""
+    mode, splits, launches = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    check(lib().fmlp_bwd_plan(H, B, D, E, dtype_code, workspace_bytes, ctypes.byref(mode), ctypes.byref(splits),
+                              ctypes.byref(launches)), "fmlp_bwd_plan")
+    return mode.value, splits.value, launches.value

@@ -10,7 +10,9 @@ sm_100a kernels); there is no other compute path.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import threading
 from typing import Tuple
 
 import numpy as np
@@ -58,6 +60,30 @@ def _check_tensors(*ts: torch.Tensor) -> torch.device:
 
 def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
     return ctypes.c_void_p(t.data_ptr())
+
+
+_LOW_MEMORY = threading.local()
+
+
+@contextlib.contextmanager
+def low_memory_backward(enabled: bool = True):
+    """Within this context (per thread) the backward entry points ask the library for its
+    least workspace (fmlp_bwd_workspace_size_min), which selects the recompute mode: the dX
+    programs recompute Z and dH rather than read the dZ^T tiles that the dW programs store
+    in the dZ-store mode. It saves that transient (2*H*E*B bytes, 8 GiB for 32 heads with
+    B = 65536 and E = 2048) at the cost of the recomputed products."""
+    prev = getattr(_LOW_MEMORY, "on", False)
+    _LOW_MEMORY.on = bool(enabled)
+    try:
+        yield
+    finally:
+        _LOW_MEMORY.on = prev
+
+
+def _bwd_workspace_bytes(L, H: int, B: int, D: int, E: int, dt: int) -> int:
+    if getattr(_LOW_MEMORY, "on", False):
+        return int(L.fmlp_bwd_workspace_size_min(H, B, D, E, dt))
+    return int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
 
 
 def flashmlp_fwd(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
@@ -130,8 +156,9 @@ def flashmlp_bwd(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     L = _lib.lib()
     dt = _dtype_code(x)
     with torch.cuda.device(dev):
-        # scratch for the fp32 dW partial sums of split dW programs (0 bytes for most shapes)
-        ws_bytes = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
+        # scratch: the dZ^T tiles of the dZ-store mode and/or the fp32 dW partial sums of
+        # split dW programs
+        ws_bytes = _bwd_workspace_bytes(L, H, B, D, E, dt)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
         stream = torch.cuda.current_stream(dev).cuda_stream
         rc = L.fmlp_bwd(_ptr(x), _ptr(w1), _ptr(w2), _ptr(do), _ptr(dx), _ptr(dw1), _ptr(dw2),
@@ -169,7 +196,7 @@ def flashmlp_bwd_dw_f32(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, do:
     L = _lib.lib()
     dt = _dtype_code(x)
     with torch.cuda.device(dev):
-        ws_bytes = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
+        ws_bytes = _bwd_workspace_bytes(L, H, B, D, E, dt)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
         stream = torch.cuda.current_stream(dev).cuda_stream
         rc = L.fmlp_bwd_dw_f32(_ptr(x), _ptr(w1), _ptr(w2), _ptr(do), _ptr(dx), _ptr(dw_out),
@@ -220,7 +247,7 @@ def flashmlp_bwd_shared_x(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, d
     L = _lib.lib()
     dt = _dtype_code(x)
     with torch.cuda.device(dev):
-        ws_bytes = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
+        ws_bytes = _bwd_workspace_bytes(L, H, B, D, E, dt)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
         stream = torch.cuda.current_stream(dev).cuda_stream
         rc = L.fmlp_bwd_shared_x(_ptr(x), _ptr(w1), _ptr(w2), _ptr(do), _ptr(dx), _ptr(dw1), _ptr(dw2),

@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(576, 1)
                     const __grid_constant__ CUtensorMap tm_w1,
                     const __grid_constant__ CUtensorMap tm_w2, T* __restrict__ dX,
                     T* __restrict__ dW1, T* __restrict__ dW2, float* __restrict__ part,
-                    int splits, int H, int B, int D, int E, uint32_t* status) {
+                    T* __restrict__ dzt, int splits, int H, int B, int D, int E, uint32_t* status) {
   using C = BwdCfg<DP>;
   using St = ActState<T, ACT>;
   constexpr int BM = C::BM;
@@ -226,6 +226,13 @@ __global__ void __launch_bounds__(576, 1)
                                st[17 + 2 * i]);
     if (pack_h) tmem_st8(col + 8, ph);
   };
+  // 16 packed 16-bit values (16 consecutive b of this thread's dZ^T row) to the dZ-store
+  // workspace: two 16-byte pieces, 8 b each, which the tiled layout keeps 512 elements
+  // (one 8-b group of 64 e rows) apart
+  auto store_dz = [](T* g, const uint32_t (&p)[8]) {
+    *reinterpret_cast<uint4*>(g) = make_uint4(p[0], p[1], p[2], p[3]);
+    *reinterpret_cast<uint4*>(g + 512) = make_uint4(p[4], p[5], p[6], p[7]);
+  };
   // dH as phase 2 uses it: with a shared input the upstream gradient of the head mean is
   // dO / H, applied here in fp32 (dH is linear in dO).
   auto dh_in = [&](uint32_t v) -> float {
@@ -233,8 +240,9 @@ __global__ void __launch_bounds__(576, 1)
     return __uint_as_float(v);
   };
   // Phase 2 over the 32 dH columns at `src`: dZ packed into the 16 columns at `dst`
-  // (`dst` == `src`, or columns this warp has already read in phase 1).
-  auto phase2 = [&](uint32_t src, uint32_t dst, const St (&st)[32]) {
+  // (`dst` == `src`, or columns this warp has already read in phase 1), and, if `g` is
+  // set, the same 32 16-bit values stored to the dZ-store workspace at g.
+  auto phase2 = [&](uint32_t src, uint32_t dst, const St (&st)[32], T* g) {
     uint32_t va[16], vb[16], pd[8];
     tmem_ld16_async(src, va);
     tmem_wait_ld_dep(va);
@@ -243,12 +251,14 @@ __global__ void __launch_bounds__(576, 1)
     for (int i = 0; i < 8; ++i)
       pd[i] = grad_pair<T, ACT>(dh_in(va[2 * i]), dh_in(va[2 * i + 1]), st[2 * i], st[2 * i + 1]);
     tmem_st8(dst, pd);
+    if (g != nullptr) store_dz(g, pd);
     tmem_wait_ld_dep(vb);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       pd[i] = grad_pair<T, ACT>(dh_in(vb[2 * i]), dh_in(vb[2 * i + 1]), st[16 + 2 * i],
                                 st[17 + 2 * i]);
     tmem_st8(dst + 8, pd);
+    if (g != nullptr) store_dz(g + 1024, pd);
   };
   auto signal = [&](uint64_t* bar, bool wrote_tmem) {
     if (wrote_tmem) tmem_wait_st();
@@ -398,6 +408,15 @@ __global__ void __launch_bounds__(576, 1)
       // Activation warps: B columns [32j, 32j+32) of Z^T / dH^T.
       const uint32_t zt = tmem + lane_off + C::W_TM_ZT + 32 * j;
       const uint32_t dt = tmem + lane_off + C::W_TM_DHT + 32 * j;
+      // dZ-store mode: the dZ^T tile of (head h, E chunk c, B tile t) is 128 x 128 values
+      // at tile index (h*nE + c)*nB + t, laid out [e / 64][b / 8][e % 64][b % 8]: a warp's
+      // 32 lanes (consecutive e) store 512 contiguous bytes per 8-b group, and each half
+      // (64 e) is the no-swizzle MN-major operand layout the dX GEMM reads with one bulk
+      // copy. This thread (e = 32q + lane) owns b = 32j..32j+31: 8-b groups 4j..4j+3. The
+      // workspace holds at most 2^32 elements, so a 32-bit element offset addresses it.
+      const uint32_t dz_off = uint32_t(((size_t(h) * nE + c) * nB + bt0) * (BM * 128)) + (q >> 1) * 8192 +
+                              (4 * j) * 512 + ((q & 1) * 32 + lane) * 8;
+      auto dz_at = [&](int bt) -> T* { return dzt == nullptr ? nullptr : dzt + (dz_off + uint32_t(bt) * (BM * 128)); };
       bool ok = true;
       for (int bt = 0; bt < nT && ok && kFused; ++bt) {
         St st[32];
@@ -424,6 +443,7 @@ __global__ void __launch_bounds__(576, 1)
           // dH^T columns [0,16) of this slice -> registers, then H^T packed over them;
           // columns [16,32) -> registers, then dZ^T packed over them
           uint32_t v[16], pd[8];
+          T* g = dz_at(bt);
           tmem_ld16_sync(dt, v);
           tmem_st16(dt, hp);
 #pragma unroll
@@ -431,10 +451,12 @@ __global__ void __launch_bounds__(576, 1)
             pd[i] = grad_pair<T, ACT>(dh_in(v[2 * i]), dh_in(v[2 * i + 1]), st[2 * i], st[2 * i + 1]);
           tmem_ld16_sync(dt + 16, v);
           tmem_st8(dt + 16, pd);
+          if (g != nullptr) store_dz(g, pd);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
             pd[i] = grad_pair<T, ACT>(dh_in(v[2 * i]), dh_in(v[2 * i + 1]), st[16 + 2 * i], st[17 + 2 * i]);
           tmem_st8(dt + 24, pd);
+          if (g != nullptr) store_dz(g + 1024, pd);
         }
         signal(&a_full[1], true);
       }
@@ -446,7 +468,7 @@ __global__ void __launch_bounds__(576, 1)
         signal(&a_full[0], true);
         if (!(ok = mbar_wait(&p_full[1], bt & 1, ctx))) break;
         tc_fence_after();
-        phase2(dt, dt, st);  // dZ^T packed over dH^T
+        phase2(dt, dt, st, dz_at(bt));  // dZ^T packed over dH^T
         signal(&a_full[1], true);
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
@@ -661,7 +683,7 @@ __global__ void __launch_bounds__(576, 1)
         phase1(zc, st, false);  // derivative state only
         if (!(ok = mbar_wait(&p_full[1], c & 1, ctx))) break;
         tc_fence_after();
-        phase2(da, zc, st);  // dZ packed over this warp's Z columns
+        phase2(da, zc, st, nullptr);  // dZ packed over this warp's Z columns
         signal(&a_full[1], true);
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
@@ -730,14 +752,17 @@ static cudaError_t launch_bwd_sx(const BwdLaunch& a) {
   const int nE = (a.E + C::ET - 1) / C::ET;
   const int splits = a.splits < 1 ? 1 : a.splits;
   if (splits > 1 && (a.part == nullptr || splits > nB)) return cudaErrorInvalidValue;
-  const long long grid = (long long)a.H * nE * splits + (SX ? 1LL : (long long)a.H) * nB;
+  // dZ-store mode: dW programs only; their dZ^T feeds fmlp_dx_gemm_kernel
+  const bool dz = a.dzt != nullptr;
+  const long long grid = (long long)a.H * nE * splits + (dz ? 0LL : (SX ? 1LL : (long long)a.H) * nB);
   if (grid <= 0 || grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   // the dW programs' fp32 target: the split partials, or the fp32 output itself
   float* kpart = splits > 1 ? a.part : a.dw_f32;
   kern<<<unsigned(grid), C::NUM_THREADS, C::SMEM, a.stream>>>(
       a.tm_x, a.tm_do, a.tm_w1, a.tm_w2, reinterpret_cast<T*>(a.dx), reinterpret_cast<T*>(a.dw1),
-      reinterpret_cast<T*>(a.dw2), kpart, splits, a.H, a.B, a.D, a.E, a.status);
+      reinterpret_cast<T*>(a.dw2), kpart, reinterpret_cast<T*>(a.dzt), splits, a.H, a.B, a.D, a.E, a.status);
   cudaError_t le = cudaGetLastError();
+  if (le == cudaSuccess && dz) le = launch_dx_gemm(a);
   if (le != cudaSuccess || splits == 1) return le;
   const long long n4 = (long long)a.H * a.D * a.E / 4;  // E % 8 == 0
   long long blocks = (n4 + 255) / 256;
@@ -786,6 +811,42 @@ int bwd_dw_splits(int H, int B, int D, int E, int sm_count) {
 size_t bwd_workspace_bytes(int H, int B, int D, int E, int sm_count) {
   const int s = bwd_dw_splits(H, B, D, E, sm_count);
   return s > 1 ? size_t(2) * s * size_t(H) * D * E * sizeof(float) : 0;
+}
+
+size_t bwd_dz_bytes(int H, int B, int D, int E, int sm_count) {
+  if (D > 128 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 0;
+  const size_t nB = (size_t(B) + kRows - 1) / kRows, nE = (size_t(E) + kBwdEt - 1) / kBwdEt;
+  const size_t bytes = size_t(H) * nE * kBwdEt * nB * kRows * 2;
+  return bytes <= kDzCapBytes ? bytes : 0;
+}
+
+int bwd_dz_splits(int H, int B, int D, int E, int sm_count) {
+  if (D > 128 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 1;
+  const long long nB = (B + kRows - 1) / kRows, nE = (E + kBwdEt - 1) / kBwdEt;
+  // The launch holds dW programs only, all of the same length, so it runs in whole waves
+  // of sm_count programs: pick S (1..8, at least 2 B tiles per split) minimising
+  // waves * tiles per program * tile time + the fp32 reduce of the partials (S > 1).
+  const int dp = D <= 64 ? 64 : 128;
+  const double tile_s = 8.0 * 128 * 128 * dp / (1.2e15 / sm_count);  // 4 products of 128x128xDP
+  const double hde = double(H) * D * E;
+  const long long max_s = nB / 2 < 8 ? nB / 2 : 8;
+  int best = 1;
+  double best_t = 0;
+  for (long long s = 1; s <= (max_s < 1 ? 1 : max_s); ++s) {
+    const long long progs = (long long)H * nE * s;
+    const long long waves = (progs + sm_count - 1) / sm_count;
+    double t = double(waves) * double((nB + s - 1) / s) * tile_s;
+    if (s > 1) t += (8.0 * s + 4.0) * hde / 6.0e12 + 5e-6;
+    if (s == 1 || t < best_t) best = int(s), best_t = t;
+  }
+  return best;
+}
+
+size_t bwd_dz_workspace_bytes(int H, int B, int D, int E, int sm_count) {
+  const size_t dz = bwd_dz_bytes(H, B, D, E, sm_count);
+  if (dz == 0) return 0;
+  const int s = bwd_dz_splits(H, B, D, E, sm_count);
+  return dz + (s > 1 ? size_t(2) * s * size_t(H) * D * E * sizeof(float) : 0);
 }
 
 int bwd_smem_bytes(int dp) {

@@ -209,12 +209,44 @@ int fmlp_fwd_shared_x(const void* x, const void* w1, const void* w2, void* o, in
   return fwd_impl(x, w1, w2, o, H, B, D, E, dtype, act, 1, stream);
 }
 
-size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {
+size_t fmlp_bwd_workspace_size_min(int H, int B, int D, int E, int dtype) {
   if (check_common(H, B, D, E, dtype) || D % 16 != 0 || D > 256 || E % 8 != 0) return 0;
   if (dtype == FMLP_DTYPE_F32) return 0;  // the fp32 backward does not split its dW programs
   DeviceInfo* dev = nullptr;
   if (device_info(&dev)) return 0;
   return bwd_workspace_bytes(H, B, D, E, dev->sm_count);
+}
+
+size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {
+  const size_t least = fmlp_bwd_workspace_size_min(H, B, D, E, dtype);
+  if (dtype == FMLP_DTYPE_F32 || D > 128 || check_common(H, B, D, E, dtype) || D % 16 != 0 || E % 8 != 0)
+    return least;
+  DeviceInfo* dev = nullptr;
+  if (device_info(&dev)) return 0;
+  const size_t dz = bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count);
+  return dz ? dz : least;
+}
+
+int fmlp_bwd_plan(int H, int B, int D, int E, int dtype, size_t workspace_bytes, int* mode, int* splits,
+                  int* launches) {
+  int rc = check_common(H, B, D, E, dtype);
+  if (rc) return rc;
+  const bool f32 = dtype == FMLP_DTYPE_F32;
+  if (D % 16 != 0 || D > (f32 ? 128 : 256)) return FMLP_ERR_UNSUPPORTED_D;
+  if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+  // the same choice as bwd_impl makes for a non-null, 16-byte aligned workspace
+  const size_t ws_need = f32 ? 0 : bwd_workspace_bytes(H, B, D, E, dev->sm_count);
+  const size_t ws_dz = (f32 || D > 128) ? 0 : bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count);
+  const bool dz = ws_dz != 0 && workspace_bytes >= ws_dz;
+  if (!dz && workspace_bytes < ws_need) return FMLP_ERR_WORKSPACE;
+  const int s = dz ? bwd_dz_splits(H, B, D, E, dev->sm_count) : (ws_need ? bwd_dw_splits(H, B, D, E, dev->sm_count) : 1);
+  const bool empty = H == 0 || B == 0 || D == 0 || E == 0;
+  if (mode) *mode = dz ? 1 : 0;
+  if (splits) *splits = s;
+  if (launches) *launches = empty ? 0 : 1 + (dz ? 1 : 0) + (s > 1 ? 1 : 0);
+  return FMLP_OK;
 }
 
 }  // extern "C"
@@ -225,7 +257,7 @@ namespace {
 // fp32 into dwf = dW1 (H,D,E) followed by dW2 (H,E,D)).
 int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1, void* dw2,
              float* dwf, void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype, int act,
-             int shared_x, void* stream) {
+             int shared_x, void* stream, bool allow_dz = true) {
   int rc = check_common(H, B, D, E, dtype);
   if (rc) return rc;
   const bool f32 = dtype == FMLP_DTYPE_F32;
@@ -236,7 +268,11 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
   const size_t ws_need = f32 ? 0 : bwd_workspace_bytes(H, B, D, E, dev->sm_count);
-  if (workspace_bytes < ws_need || (ws_need && (workspace == nullptr || !aligned16(workspace))))
+  // dZ-store mode when the workspace holds dZ^T (the size fmlp_bwd_workspace_size asks
+  // for); otherwise the dX programs recompute Z and dH (needs ws_need bytes at least)
+  const size_t ws_dz = (f32 || D > 128 || !allow_dz) ? 0 : bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count);
+  const bool dz_mode = ws_dz != 0 && workspace_bytes >= ws_dz && workspace != nullptr && aligned16(workspace);
+  if (!dz_mode && (workspace_bytes < ws_need || (ws_need && (workspace == nullptr || !aligned16(workspace)))))
     return FMLP_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (H == 0 || D == 0) return FMLP_OK;
@@ -278,8 +314,15 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
   a.x = x, a.w1 = w1;
   a.dx = dx, a.dw1 = dw1, a.dw2 = dw2;
   a.dw_f32 = dwf;
-  a.splits = ws_need ? bwd_dw_splits(H, B, D, E, dev->sm_count) : 1;
-  a.part = ws_need ? static_cast<float*>(workspace) : nullptr;
+  if (dz_mode) {
+    const size_t dz = bwd_dz_bytes(H, B, D, E, dev->sm_count);
+    a.dzt = workspace;
+    a.splits = bwd_dz_splits(H, B, D, E, dev->sm_count);
+    a.part = a.splits > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + dz) : nullptr;
+  } else {
+    a.splits = ws_need ? bwd_dw_splits(H, B, D, E, dev->sm_count) : 1;
+    a.part = ws_need ? static_cast<float*>(workspace) : nullptr;
+  }
   a.sm_count = dev->sm_count;
   a.H = H, a.B = B, a.D = D, a.E = E;
   a.bf16 = bf;
@@ -300,6 +343,19 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
   return bwd_impl(x, w1, w2, dO, dx, dw1, dw2, nullptr, workspace, workspace_bytes, H, B, D, E, dtype, act, 0,
                   stream);
 }
+
+}  // extern "C"
+
+namespace fmlp {
+int bwd_entry(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1, void* dw2,
+              void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype, int act,
+              void* stream, int allow_dz) {
+  return bwd_impl(x, w1, w2, dO, dx, dw1, dw2, nullptr, workspace, workspace_bytes, H, B, D, E, dtype, act, 0,
+                  stream, allow_dz != 0);
+}
+}  // namespace fmlp
+
+extern "C" {
 
 int fmlp_bwd_shared_x(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1,
                       void* dw2, void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype,

@@ -43,6 +43,7 @@ struct BwdLaunch {
   void* dw2;
   float* part;         // fp32 dW partial sums of split dW programs (splits > 1), else null
   float* dw_f32;       // if set: dW1 (H,D,E) then dW2 (H,E,D) as unrounded fp32, not dw1/dw2
+  void* dzt;           // dZ-store mode: dZ^T tiles (H, nE, nB) x 128 x 128 in the input dtype
   const Tf32BwdMaps* tf32_maps;  // fp32 inputs only
   int splits;          // dW programs per (head, E chunk); 1 = no split (DP <= 128 only)
   int sm_count;
@@ -66,6 +67,7 @@ cudaError_t launch_fwd(const FwdLaunch& a);       // picks the kernel for a.dp
 cudaError_t launch_fwd_pair(const FwdLaunch& a);  // two row tiles per CTA, D <= 128
 cudaError_t launch_bwd(const BwdLaunch& a);     // picks the kernel for a.dp
 cudaError_t launch_bwd256(const BwdLaunch& a);  // 128 < D <= 256
+cudaError_t launch_dx_gemm(const BwdLaunch& a);  // dX from the stored dZ^T (dZ-store mode)
 cudaError_t launch_fwd_tf32(const FwdLaunch& a);  // fp32 inputs, TF32 products, D <= 128
 cudaError_t launch_bwd_tf32(const BwdLaunch& a);
 int bwd256_smem_bytes();
@@ -76,5 +78,21 @@ int current_device_status(int* sm_count, uint32_t** status);
 // bytes it needs: 2 * splits * H * D * E * 4 when splits > 1.
 int bwd_dw_splits(int H, int B, int D, int E, int sm_count);
 size_t bwd_workspace_bytes(int H, int B, int D, int E, int sm_count);
+
+// dZ-store mode of the 16-bit backward with D <= 128: the dW programs also store dZ^T and
+// a GEMM over E forms dX from it (fmlp_dxgemm.cu). bwd_dz_bytes is the dZ^T workspace
+// (0 when the mode does not apply or would need more than kDzCapBytes);
+// bwd_dz_splits the dW split factor of that launch, whose fp32 partials follow the dZ^T
+// region (bwd_dz_workspace_bytes is the total).
+constexpr size_t kDzCapBytes = size_t(8) << 30;
+size_t bwd_dz_bytes(int H, int B, int D, int E, int sm_count);
+int bwd_dz_splits(int H, int B, int D, int E, int sm_count);
+size_t bwd_dz_workspace_bytes(int H, int B, int D, int E, int sm_count);
+
+// Body of fmlp_bwd; allow_dz = 0 keeps the recompute mode whatever the workspace size
+// (fmlp_bwd_noalloc).
+int bwd_entry(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1, void* dw2,
+              void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype, int act,
+              void* stream, int allow_dz);
 
 }  // namespace fmlp

@@ -25,6 +25,7 @@
 #include <mutex>
 
 #include "../../include/flashmlp_b200.h"
+#include "fmlp_kernels.h"
 
 namespace fmlp {
 namespace {
@@ -61,13 +62,13 @@ extern "C" int fmlp_bwd_noalloc(const void* x, const void* w1, const void* w2, c
                                 void* dx, void* dw1, void* dw2, int H, int B, int D, int E,
                                 int dtype, int act, void* stream) {
   static_assert(fmlp::kNoAllocScratchBytes == FMLP_NOALLOC_SCRATCH_BYTES, "header and array agree");
-  const size_t need = fmlp_bwd_workspace_size(H, B, D, E, dtype);
+  const size_t need = fmlp_bwd_workspace_size_min(H, B, D, E, dtype);
   if (need > fmlp::kNoAllocScratchBytes) return FMLP_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   if (need > 0) {
     const int rc = fmlp::scratch_for_current_device(&scratch);
     if (rc) return rc;
   }
-  return fmlp_bwd(x, w1, w2, dO, dx, dw1, dw2, scratch, need > 0 ? fmlp::kNoAllocScratchBytes : 0, H, B,
-                  D, E, dtype, act, stream);
+  return fmlp::bwd_entry(x, w1, w2, dO, dx, dw1, dw2, scratch, need > 0 ? fmlp::kNoAllocScratchBytes : 0, H, B,
+                         D, E, dtype, act, stream, 0);
 }

@@ -126,6 +126,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// Untiled bulk copy of `bytes` contiguous bytes from global to shared memory (both
+// addresses 16-byte aligned, size a multiple of 16); completion as transaction bytes.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Makes generic-proxy shared-memory writes visible to the async proxy (tensor core).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -353,6 +363,20 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_
   d |= uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= uint64_t(1) << 46;
   d |= uint64_t(2) << 61;
+  return d;
+}
+
+// Shared-memory matrix descriptor without swizzle (layout type 0): the operand is tiled
+// in 8 x 16-byte core matrices of 128 contiguous bytes. For an MN-major 16-bit operand a
+// core matrix holds 8 MN elements (16 B) in each of 8 consecutive K rows; LBO is the byte
+// distance between core matrices adjacent in K, SBO between those adjacent in MN.
+__device__ __forceinline__ uint64_t make_sdesc_noswz(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                     uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= uint64_t((smem_addr >> 4) & 0x3FFFu);
+  d |= uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;
   return d;
 }
 

@@ -98,13 +98,33 @@ int fmlp_bwd_dw_f32(const void* x, const void* w1, const void* w2, const void* d
                     float* dw_f32, void* workspace, size_t workspace_bytes, int H, int B, int D,
                     int E, int dtype, int act, void* stream);
 
-/* Device scratch bytes fmlp_bwd needs for this shape on the current device (no reference
- * counterpart; the reference allocates its outputs with torch.zeros_like,
- * flashmlp.py:516-518). Nonzero only when the launch has too few (head, E chunk) pairs to
- * fill the GPU (e.g. 4 heads with E = 2048 on a 148-SM B200): the dW programs are then
- * split over B ranges and their fp32 partial sums (2 * splits * H * D * E floats) are added
- * in a fixed order by a second kernel. Returns 0 for invalid arguments. */
+/* Device scratch bytes for fmlp_bwd on the current device (no reference counterpart; the
+ * reference allocates its outputs with torch.zeros_like, flashmlp.py:516-518).
+ *
+ * fmlp_bwd_workspace_size: the workspace of the fastest mode. For 16-bit inputs with
+ * D <= 128 that is the dZ-store mode: the dW programs also store their rounded dZ^T tiles
+ * (H * ceil(E/128)*128 * ceil(B/128)*128 16-bit values, at most 8 GiB) and dX becomes a
+ * GEMM over E of those tiles instead of programs that recompute Z and dH; plus the fp32
+ * dW partial sums below when that launch splits its dW programs.
+ *
+ * fmlp_bwd_workspace_size_min: the least workspace fmlp_bwd accepts (the recompute mode).
+ * Nonzero only when the launch has too few (head, E chunk) pairs to fill the GPU (e.g. 4
+ * heads with E = 2048 on a 148-SM B200): the dW programs are then split over B ranges and
+ * their fp32 partial sums (2 * splits * H * D * E floats) are added in a fixed order by a
+ * second kernel.
+ *
+ * fmlp_bwd picks the dZ-store mode when workspace_bytes >= fmlp_bwd_workspace_size and
+ * the mode applies, otherwise the recompute mode. Both return 0 for invalid arguments. */
 size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype);
+size_t fmlp_bwd_workspace_size_min(int H, int B, int D, int E, int dtype);
+
+/* What fmlp_bwd runs for this shape and workspace size on the current device (no reference
+ * counterpart): *mode 1 = dZ-store mode, 0 = recompute mode; *splits = dW programs per
+ * (head, E chunk); *launches = kernels per call (the backward kernel, the dX GEMM in the
+ * dZ-store mode, the dW partial reduction when *splits > 1). Any output may be NULL.
+ * Returns FMLP_ERR_WORKSPACE when workspace_bytes is below fmlp_bwd_workspace_size_min. */
+int fmlp_bwd_plan(int H, int B, int D, int E, int dtype, size_t workspace_bytes, int* mode, int* splits,
+                  int* launches);
 
 /*
  * Unified backward that allocates nothing: same arguments and results as fmlp_bwd, minus
@@ -113,8 +133,9 @@ size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype);
  * outputs, or processes whose allocator already holds the GPU's memory. The fp32 dW
  * partial sums that fmlp_bwd keeps in the caller's workspace live instead in a static
  * device array of FMLP_NOALLOC_SCRATCH_BYTES, which every GPU that loads the library holds
- * until the process exits; a shape whose fmlp_bwd_workspace_size exceeds it returns
- * FMLP_ERR_SCRATCH_LIMIT (no D <= 256 shape does on a 148-SM B200).
+ * until the process exits; a shape whose fmlp_bwd_workspace_size_min exceeds it returns
+ * FMLP_ERR_SCRATCH_LIMIT (no D <= 256 shape does on a 148-SM B200). It always runs the
+ * recompute mode (dX programs recompute Z and dH), never the dZ-store mode.
  * The first call on a device whose shape needs scratch looks up the array's device
  * address (cudaGetSymbolAddress); make that first call before any stream capture on the
  * device. All calls on a device share the array: calls whose kernels overlap on the GPU

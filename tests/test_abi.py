@@ -61,7 +61,10 @@ def test_argument_validation_without_device():
     assert L.fmlp_bwd(nul, nul, nul, nul, nul, nul, nul, nul, 0, 1, 128, 272, 64, 1, 0, nul) == d["FMLP_ERR_UNSUPPORTED_D"]
     assert L.fmlp_sgd_update(nul, nul, -5, 0.1, 1, nul) == d["FMLP_ERR_INVALID_SHAPE"]
     assert L.fmlp_sgd_update(nul, nul, 5, 0.1, 3, nul) == d["FMLP_ERR_UNSUPPORTED_DTYPE"]
-    assert L.fmlp_bwd_workspace_size(32, 65536, 128, 2048, 1) == 0
+    assert L.fmlp_bwd_workspace_size(32, 65536, 128, 2048, 1) == 0  # no device here
+    assert L.fmlp_bwd_workspace_size_min(32, 65536, 128, 2048, 1) == 0
+    assert L.fmlp_bwd_plan(1, 128, 72, 64, 1, 0, None, None, None) == d["FMLP_ERR_UNSUPPORTED_D"]
+    assert L.fmlp_bwd_plan(1, 128, 64, 100, 1, 0, None, None, None) == d["FMLP_ERR_UNSUPPORTED_E"]
     assert L.fmlp_bwd_noalloc(nul, nul, nul, nul, nul, nul, nul, 1, 128, 272, 64, 1, 0, nul) == d["FMLP_ERR_UNSUPPORTED_D"]
 
 

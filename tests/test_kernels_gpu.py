@@ -141,10 +141,11 @@ def test_d256_vs_oracle():
 
 
 # ----------------------------------------------------------------------------- split dW programs
+# (recompute mode, selected by the least workspace; the dZ-store mode has its own file)
 def _ws_bytes(H, B, D, E, dt):
     from flashmlp_b200 import _lib
     code = _lib.FMLP_DTYPE_BF16 if dt == torch.bfloat16 else _lib.FMLP_DTYPE_F16
-    return int(_lib.lib().fmlp_bwd_workspace_size(H, B, D, E, code))
+    return int(_lib.lib().fmlp_bwd_workspace_size_min(H, B, D, E, code))
 
 
 @pytest.mark.parametrize("shape,dtype", [((2, 1000, 96, 200), "bf16"), ((1, 2048, 128, 256), "f16"),
@@ -161,7 +162,8 @@ def test_split_dw_vs_oracle(shape, dtype):
     x, w1, w2, do = (torch.from_numpy(a).to(dt).cuda() for a in xs)
     atol, rtol = tol_for(dt, "bwd")
     for act in ACTS:
-        got = [to_np(t) for t in F().flashmlp_bwd(x, w1, w2, do, act)]
+        with F().low_memory_backward():
+            got = [to_np(t) for t in F().flashmlp_bwd(x, w1, w2, do, act)]
         want = orc.bwd_kernel(*xs, act, dtype)
         for name, a, r in zip(("dx", "dw1", "dw2"), got, want):
             np.testing.assert_allclose(a, r, atol=atol, rtol=rtol, err_msg=f"{shape} {act} {name}")
@@ -175,9 +177,10 @@ def test_split_dw_matches_unsplit_launch():
     dt = torch.bfloat16
     assert _ws_bytes(2, B, D, E, dt) > 0 and _ws_bytes(H, B, D, E, dt) == 0
     x, w1, w2, do = make_inputs(H, B, D, E, dt, seed=21)
-    big = F().flashmlp_bwd(x, w1, w2, do, "silu")
-    small = F().flashmlp_bwd(x[:2].contiguous(), w1[:2].contiguous(), w2[:2].contiguous(),
-                             do[:2].contiguous(), "silu")
+    with F().low_memory_backward():
+        big = F().flashmlp_bwd(x, w1, w2, do, "silu")
+        small = F().flashmlp_bwd(x[:2].contiguous(), w1[:2].contiguous(), w2[:2].contiguous(),
+                                 do[:2].contiguous(), "silu")
     assert torch.equal(big[0][:2], small[0])
     refs = ref_bwd(x[:2], w1[:2], w2[:2], do[:2], "silu")
     for k, i in (("dw1", 1), ("dw2", 2)):
@@ -222,7 +225,8 @@ def test_workspace_too_small_is_rejected():
     assert L.fmlp_bwd(*args, None, need, H, B, D, E, 1, 2, None) == 9
     assert L.fmlp_bwd(*args, p(ws), need, H, B, D, E, 1, 2, None) == 0
     torch.cuda.synchronize()
-    assert torch.equal(outs[1], F().flashmlp_bwd(x, w1, w2, do, "silu")[1])
+    with F().low_memory_backward():
+        assert torch.equal(outs[1], F().flashmlp_bwd(x, w1, w2, do, "silu")[1])
 
 
 # ----------------------------------------------------------------------------- BASELINE configs

@@ -78,7 +78,7 @@ def test_shared_input_deterministic_and_split_dw():
     from flashmlp_b200 import _lib
 
     H, B, D, E = 2, 4096, 128, 256
-    assert _lib.lib().fmlp_bwd_workspace_size(H, B, D, E, 1) > 0  # dW programs split over B
+    assert _lib.lib().fmlp_bwd_workspace_size_min(H, B, D, E, 1) > 0  # dW programs split over B
     x, w1, w2, do = _shared_inputs(H, B, D, E, torch.bfloat16, 9)
     a = F().flashmlp_bwd_shared_x(x, w1, w2, do, "sigmoid")
     b = F().flashmlp_bwd_shared_x(x, w1, w2, do, "sigmoid")

@@ -30,7 +30,7 @@ def test_bwd_noalloc_matches_bwd_on_two_calls_in_a_row():
     L = _lib.lib()
     H, B, D, E = 4, 4096, 128, 1024
     dt = torch.bfloat16
-    need = int(L.fmlp_bwd_workspace_size(H, B, D, E, _lib.FMLP_DTYPE_BF16))
+    need = int(L.fmlp_bwd_workspace_size_min(H, B, D, E, _lib.FMLP_DTYPE_BF16))
     assert 0 < need <= (32 << 20), "shape chosen so that the backward uses scratch memory"
     p = lambda t: ctypes.c_void_p(t.data_ptr())
     for seed, act in ((31, "silu"), (32, "sigmoid")):
