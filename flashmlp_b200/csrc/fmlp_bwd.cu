@@ -814,7 +814,7 @@ size_t bwd_workspace_bytes(int H, int B, int D, int E, int sm_count) {
 }
 
 size_t bwd_dz_bytes(int H, int B, int D, int E, int sm_count) {
-  if (D > 128 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 0;
+  if (D > 256 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 0;
   const size_t nB = (size_t(B) + kRows - 1) / kRows, nE = (size_t(E) + kBwdEt - 1) / kBwdEt;
   const size_t bytes = size_t(H) * nE * kBwdEt * nB * kRows * 2;
   return bytes <= kDzCapBytes ? bytes : 0;

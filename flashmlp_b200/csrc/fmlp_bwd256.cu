@@ -32,6 +32,9 @@
 //
 // Warp roles as in fmlp_bwd.cu: warp 0 TMA, warp 1 MMA, warps 2..17 activation (warp
 // (q, j) owns TMEM lanes [32q, 32q+32) and 16-column slice j of each 64-column product).
+//
+// dZ-store mode (as in fmlp_bwd.cu): the launch holds only the dW programs, those of D half
+// 0 also store their packed dZ^T tiles, and fmlp_dx_gemm_kernel (N = 256) forms dX.
 #include "fmlp_act.cuh"
 #include "fmlp_kernels.h"
 #include "fmlp_ptx.cuh"
@@ -82,8 +85,8 @@ __global__ void __launch_bounds__(576, 1)
                        const __grid_constant__ CUtensorMap tm_w1,
                        const __grid_constant__ CUtensorMap tm_w2, const T* __restrict__ X,
                        const T* __restrict__ W1, T* __restrict__ dX, T* __restrict__ dW1,
-                       T* __restrict__ dW2, float* __restrict__ dwf, int H, int B, int D, int E,
-                       uint32_t* status) {
+                       T* __restrict__ dW2, float* __restrict__ dwf, T* __restrict__ dzt, int H, int B,
+                       int D, int E, uint32_t* status) {
   using C = Bwd256Cfg;
   using St = ActState<T, ACT>;
   constexpr int DP = C::DP;
@@ -174,14 +177,19 @@ __global__ void __launch_bounds__(576, 1)
       p[i] = act_pair<T, ACT>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]), st[2 * i], st[2 * i + 1]);
     if (pack_h) tmem_st8(col, p);
   };
-  // Phase 2 over the 16 dH columns at `col`: dZ packed into the first 8 of them.
-  auto phase2 = [&](uint32_t col, const St (&st)[16]) {
+  // Phase 2 over the 16 dH columns at `col`: dZ packed into the first 8 of them and, if
+  // `g` is set, stored to the dZ-store workspace as two 8-value pieces at g and g + 512.
+  auto phase2 = [&](uint32_t col, const St (&st)[16], T* gz) {
     uint32_t v[16], p[8];
     tmem_ld16_sync(col, v);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       p[i] = grad_pair<T, ACT>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]), st[2 * i], st[2 * i + 1]);
     tmem_st8(col, p);
+    if (gz != nullptr) {
+      *reinterpret_cast<uint4*>(gz) = make_uint4(p[0], p[1], p[2], p[3]);
+      *reinterpret_cast<uint4*>(gz + 512) = make_uint4(p[4], p[5], p[6], p[7]);
+    }
   };
   auto signal = [&](uint64_t* bar, bool wrote_tmem) {
     if (wrote_tmem) tmem_wait_st();
@@ -326,6 +334,16 @@ __global__ void __launch_bounds__(576, 1)
       // Activation warps: B columns [16j, 16j+16) of Z^T / dH^T.
       const uint32_t zt = tmem + lane_off + C::W_TM_ZT + 16 * j;
       const uint32_t dt = tmem + lane_off + C::W_TM_DHT + 16 * j;
+      // dZ-store mode (the D-half-0 programs; both halves compute the same dZ^T): the tiled
+      // workspace of fmlp_bwd.cu, one 128 x 128 tile per (head, 128-wide E chunk, 128-row B
+      // tile) laid out [e / 64][b / 8][e % 64][b % 8]. A 64-row tile t is half (t % 2) of
+      // B tile t / 2; this thread (e = 32q + lane) owns b = 64(t%2) + 16j + 0..15: 8-b
+      // groups 8(t%2) + 2j and the next. 32-bit element offsets (the workspace holds at
+      // most 2^32 elements).
+      const int nB128 = (B + BM - 1) / BM;
+      const uint32_t dz_off = uint32_t((size_t(h) * nEw + c) * nB128 * (BM * 128)) + (q >> 1) * 8192 +
+                              (2 * j) * 512 + ((q & 1) * 32 + lane) * 8;
+      T* const dz = (g == 0) ? dzt : nullptr;
       bool ok = true;
       for (int t = 0; t < nT && ok; ++t) {
         St st[16];
@@ -335,7 +353,7 @@ __global__ void __launch_bounds__(576, 1)
         signal(&a_full[0], true);
         if (!(ok = mbar_wait(&p_full[1], t & 1, ctx))) break;
         tc_fence_after();
-        phase2(dt, st);  // dZ^T packed over dH^T
+        phase2(dt, st, dz != nullptr ? dz + (dz_off + uint32_t(t >> 1) * (BM * 128) + uint32_t(t & 1) * 4096) : nullptr);
         signal(&a_full[1], true);
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
@@ -541,7 +559,7 @@ __global__ void __launch_bounds__(576, 1)
         signal(&a_full[0], false);
         if (!(ok = mbar_wait(&p_full[1], c & 1, ctx))) break;
         tc_fence_after();
-        phase2(da, st);  // dZ packed over dH
+        phase2(da, st, nullptr);  // dZ packed over dH
         signal(&a_full[1], true);
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
@@ -577,13 +595,17 @@ static cudaError_t launch_bwd256_t(const BwdLaunch& a) {
   if (e != cudaSuccess) return e;
   const int nBx = (a.B + kRows - 1) / kRows;
   const int nEw = (a.E + C::EW - 1) / C::EW;
-  const long long grid = (long long)a.H * (2LL * nEw + nBx);
+  // dZ-store mode: dW programs only (they store dZ^T), then fmlp_dx_gemm_kernel forms dX
+  const bool dz = a.dzt != nullptr;
+  const long long grid = (long long)a.H * (2LL * nEw + (dz ? 0 : nBx));
   if (grid <= 0 || grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   kern<<<unsigned(grid), C::NUM_THREADS, C::SMEM, a.stream>>>(
       a.tm_x, a.tm_do, a.tm_w1, a.tm_w2, reinterpret_cast<const T*>(a.x), reinterpret_cast<const T*>(a.w1),
-      reinterpret_cast<T*>(a.dx), reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), a.dw_f32, a.H, a.B,
-      a.D, a.E, a.status);
-  return cudaGetLastError();
+      reinterpret_cast<T*>(a.dx), reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), a.dw_f32,
+      reinterpret_cast<T*>(a.dzt), a.H, a.B, a.D, a.E, a.status);
+  cudaError_t le = cudaGetLastError();
+  if (le == cudaSuccess && dz) le = launch_dx_gemm(a);
+  return le;
 }
 
 template <typename T>

@@ -219,7 +219,7 @@ size_t fmlp_bwd_workspace_size_min(int H, int B, int D, int E, int dtype) {
 
 size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {
   const size_t least = fmlp_bwd_workspace_size_min(H, B, D, E, dtype);
-  if (dtype == FMLP_DTYPE_F32 || D > 128 || check_common(H, B, D, E, dtype) || D % 16 != 0 || E % 8 != 0)
+  if (dtype == FMLP_DTYPE_F32 || D > 256 || check_common(H, B, D, E, dtype) || D % 16 != 0 || E % 8 != 0)
     return least;
   DeviceInfo* dev = nullptr;
   if (device_info(&dev)) return 0;
@@ -238,7 +238,7 @@ int fmlp_bwd_plan(int H, int B, int D, int E, int dtype, size_t workspace_bytes,
   if ((rc = device_info(&dev))) return rc;
   // the same choice as bwd_impl makes for a non-null, 16-byte aligned workspace
   const size_t ws_need = f32 ? 0 : bwd_workspace_bytes(H, B, D, E, dev->sm_count);
-  const size_t ws_dz = (f32 || D > 128) ? 0 : bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count);
+  const size_t ws_dz = f32 ? 0 : bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count);
   const bool dz = ws_dz != 0 && workspace_bytes >= ws_dz;
   if (!dz && workspace_bytes < ws_need) return FMLP_ERR_WORKSPACE;
   const int s = dz ? bwd_dz_splits(H, B, D, E, dev->sm_count) : (ws_need ? bwd_dw_splits(H, B, D, E, dev->sm_count) : 1);
@@ -270,7 +270,7 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
   const size_t ws_need = f32 ? 0 : bwd_workspace_bytes(H, B, D, E, dev->sm_count);
   // dZ-store mode when the workspace holds dZ^T (the size fmlp_bwd_workspace_size asks
   // for); otherwise the dX programs recompute Z and dH (needs ws_need bytes at least)
-  const size_t ws_dz = (f32 || D > 128 || !allow_dz) ? 0 : bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count);
+  const size_t ws_dz = (f32 || !allow_dz) ? 0 : bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count);
   const bool dz_mode = ws_dz != 0 && workspace_bytes >= ws_dz && workspace != nullptr && aligned16(workspace);
   if (!dz_mode && (workspace_bytes < ws_need || (ws_need && (workspace == nullptr || !aligned16(workspace)))))
     return FMLP_ERR_WORKSPACE;

@@ -21,8 +21,9 @@
 // The dW programs store each dZ^T tile (128 e x 128 b of one head, E chunk and B tile) as
 // [e / 64][b / 8][e % 64][b % 8], so the 64 e of a K step for all 128 b are 16 KB of
 // contiguous memory already in that operand layout: one untiled bulk copy per stage.
-// Three to four stages of 24-32 KB keep ~100 KB of loads in flight per CTA; two CTAs fit
-// on an SM (shared memory and TMEM), so one CTA's epilogue overlaps the other's loads.
+// Three to four stages of 24-32 KB (two of 48 KB for D = 256, N = 256) keep ~100 KB of
+// loads in flight per CTA; two CTAs fit on an SM (shared memory and TMEM), so one CTA's
+// epilogue overlaps the other's loads.
 #include "fmlp_act.cuh"
 #include "fmlp_kernels.h"
 #include "fmlp_ptx.cuh"
@@ -37,7 +38,7 @@ struct DxGemmCfg {
   static constexpr int TILE_ELEMS = BM * 128;      // one stored dZ^T tile (128 e x 128 b)
   static constexpr int B_BYTES = DP * KT * 2;      // W1: DP d rows x 64 e
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int NST = DP == 64 ? 4 : 3;
+  static constexpr int NST = DP == 64 ? 4 : (DP == 128 ? 3 : 2);
   static constexpr int OFF_BAR = NST * STAGE;
   static constexpr int OFF_MISC = OFF_BAR + (2 * NST + 2) * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + alignment slack
@@ -194,6 +195,8 @@ cudaError_t launch_dx_gemm(const BwdLaunch& a) {
   switch (a.dp) {
     case 64: return a.bf16 ? launch_dx_gemm_dt<64, __nv_bfloat16>(a) : launch_dx_gemm_dt<64, __half>(a);
     case 128: return a.bf16 ? launch_dx_gemm_dt<128, __nv_bfloat16>(a) : launch_dx_gemm_dt<128, __half>(a);
+    case 256: return a.shared_x ? cudaErrorNotSupported
+                                : (a.bf16 ? launch_dx_gemm_t<256, __nv_bfloat16, false>(a) : launch_dx_gemm_t<256, __half, false>(a));
   }
   return cudaErrorNotSupported;
 }

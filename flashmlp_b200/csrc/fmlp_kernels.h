@@ -79,7 +79,7 @@ int current_device_status(int* sm_count, uint32_t** status);
 int bwd_dw_splits(int H, int B, int D, int E, int sm_count);
 size_t bwd_workspace_bytes(int H, int B, int D, int E, int sm_count);
 
-// dZ-store mode of the 16-bit backward with D <= 128: the dW programs also store dZ^T and
+// dZ-store mode of the 16-bit backward (D <= 256): the dW programs also store dZ^T and
 // a GEMM over E forms dX from it (fmlp_dxgemm.cu). bwd_dz_bytes is the dZ^T workspace
 // (0 when the mode does not apply or would need more than kDzCapBytes);
 // bwd_dz_splits the dW split factor of that launch, whose fp32 partials follow the dZ^T

@@ -102,7 +102,7 @@ int fmlp_bwd_dw_f32(const void* x, const void* w1, const void* w2, const void* d
  * reference allocates its outputs with torch.zeros_like, flashmlp.py:516-518).
  *
  * fmlp_bwd_workspace_size: the workspace of the fastest mode. For 16-bit inputs with
- * D <= 128 that is the dZ-store mode: the dW programs also store their rounded dZ^T tiles
+ * D <= 256 that is the dZ-store mode: the dW programs also store their rounded dZ^T tiles
  * (H * ceil(E/128)*128 * ceil(B/128)*128 16-bit values, at most 8 GiB) and dX becomes a
  * GEMM over E of those tiles instead of programs that recompute Z and dH; plus the fp32
  * dW partial sums below when that launch splits its dW programs.

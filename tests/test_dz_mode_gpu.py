@@ -1,4 +1,4 @@
-"""The dZ-store mode of the unified backward (16-bit inputs, D <= 128).
+"""The dZ-store mode of the unified backward (16-bit inputs, D <= 256).
 
 With the workspace fmlp_bwd_workspace_size asks for, the dW programs also store their
 rounded dZ^T tiles and dX is a GEMM over E of those tiles (fmlp_dx_gemm_kernel) instead of
@@ -54,7 +54,8 @@ def _plan(H, B, D, E, dt, low_memory=False):
 
 
 @pytest.mark.parametrize("shape,dtype", [((2, 200, 64, 136), "bf16"), ((3, 300, 128, 264), "f16"),
-                                         ((1, 257, 96, 200), "bf16"), ((5, 130, 112, 1032), "bf16")])
+                                         ((1, 257, 96, 200), "bf16"), ((5, 130, 112, 1032), "bf16"),
+                                         ((2, 130, 256, 136), "f16"), ((1, 200, 192, 264), "bf16")])
 def test_dz_mode_vs_oracle(shape, dtype):
     from oracle import flashmlp_oracle as orc
 
@@ -72,7 +73,7 @@ def test_dz_mode_vs_oracle(shape, dtype):
 
 
 @pytest.mark.parametrize("shape,dtype", [((2, 1000, 96, 200), torch.bfloat16), ((1, 2048, 128, 256), torch.float16),
-                                         ((2, 4096, 16, 136), torch.bfloat16)])
+                                         ((2, 4096, 16, 136), torch.bfloat16), ((2, 1000, 256, 520), torch.float16)])
 def test_dz_mode_vs_torch_fp32_longer_batches(shape, dtype):
     # Over long batches dW sums many H / dZ values whose 16-bit rounding may flip against
     # an exact-activation oracle; the bound of the fp32 reference scales with that sum.
@@ -86,7 +87,8 @@ def test_dz_mode_vs_torch_fp32_longer_batches(shape, dtype):
             assert_close(got[i], *refs[k], dtype, "bwd", f"{shape} {act} {k}")
 
 
-@pytest.mark.parametrize("shape,dtype", [((8, 8192, 128, 1024), torch.bfloat16), ((6, 3000, 64, 520), torch.float16)])
+@pytest.mark.parametrize("shape,dtype", [((8, 8192, 128, 1024), torch.bfloat16), ((6, 3000, 64, 520), torch.float16),
+                                         ((3, 4096, 256, 512), torch.float16)])
 def test_dz_mode_matches_recompute_mode(shape, dtype):
     H, B, D, E = shape
     fast, slow = _plan(H, B, D, E, dtype), _plan(H, B, D, E, dtype, low_memory=True)
