@@ -94,6 +94,32 @@ size_t elem_bytes(int dtype) { return dtype == FMLP_DTYPE_F32 ? 4 : 2; }
 
 int cuda_rc(cudaError_t e) { return e == cudaSuccess ? FMLP_OK : FMLP_ERR_CUDA; }
 
+// What a backward call runs for a given workspace: the dZ-store mode when the workspace
+// holds the dZ^T tiles (and their split-dW partials) and the mode applies, otherwise the
+// recompute mode, which needs `need` bytes (0 unless its dW programs split). One rule for
+// fmlp_bwd and fmlp_bwd_plan. `usable`: the workspace pointer is non-null and 16-byte
+// aligned (fmlp_bwd_plan assumes it is).
+struct BwdPlan {
+  bool dz = false;
+  int splits = 1;
+  size_t dz_bytes = 0;  // dZ^T region at the start of the workspace (dZ-store mode)
+};
+
+int plan_bwd(int H, int B, int D, int E, bool f32, bool allow_dz, int sm_count, size_t workspace_bytes,
+             bool usable, BwdPlan* p) {
+  const size_t need = f32 ? 0 : bwd_workspace_bytes(H, B, D, E, sm_count);
+  const size_t ws_dz = (f32 || !allow_dz) ? 0 : bwd_dz_workspace_bytes(H, B, D, E, sm_count);
+  p->dz = ws_dz != 0 && workspace_bytes >= ws_dz && usable;
+  if (!p->dz && (workspace_bytes < need || (need && !usable))) return FMLP_ERR_WORKSPACE;
+  if (p->dz) {
+    p->splits = bwd_dz_splits(H, B, D, E, sm_count);
+    p->dz_bytes = bwd_dz_bytes(H, B, D, E, sm_count);
+  } else {
+    p->splits = need ? bwd_dw_splits(H, B, D, E, sm_count) : 1;
+  }
+  return FMLP_OK;
+}
+
 // w - lr * g is formed with two roundings (no FMA contraction), the same arithmetic as the
 // fused all-reduce + SGD kernel and as `w.float() - lr * g` in PyTorch.
 __global__ void sgd_kernel_bf16(__nv_bfloat16* w, const float* g, long long n, float lr) {
@@ -236,16 +262,12 @@ int fmlp_bwd_plan(int H, int B, int D, int E, int dtype, size_t workspace_bytes,
   if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
-  // the same choice as bwd_impl makes for a non-null, 16-byte aligned workspace
-  const size_t ws_need = f32 ? 0 : bwd_workspace_bytes(H, B, D, E, dev->sm_count);
-  const size_t ws_dz = f32 ? 0 : bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count);
-  const bool dz = ws_dz != 0 && workspace_bytes >= ws_dz;
-  if (!dz && workspace_bytes < ws_need) return FMLP_ERR_WORKSPACE;
-  const int s = dz ? bwd_dz_splits(H, B, D, E, dev->sm_count) : (ws_need ? bwd_dw_splits(H, B, D, E, dev->sm_count) : 1);
+  BwdPlan p;  // the choice fmlp_bwd makes for a non-null, 16-byte aligned workspace
+  if ((rc = plan_bwd(H, B, D, E, f32, true, dev->sm_count, workspace_bytes, true, &p))) return rc;
   const bool empty = H == 0 || B == 0 || D == 0 || E == 0;
-  if (mode) *mode = dz ? 1 : 0;
-  if (splits) *splits = s;
-  if (launches) *launches = empty ? 0 : 1 + (dz ? 1 : 0) + (s > 1 ? 1 : 0);
+  if (mode) *mode = p.dz ? 1 : 0;
+  if (splits) *splits = p.splits;
+  if (launches) *launches = empty ? 0 : 1 + (p.dz ? 1 : 0) + (p.splits > 1 ? 1 : 0);
   return FMLP_OK;
 }
 
@@ -267,13 +289,12 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
   if (shared_x && H == 0) return FMLP_ERR_INVALID_SHAPE;
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
-  const size_t ws_need = f32 ? 0 : bwd_workspace_bytes(H, B, D, E, dev->sm_count);
   // dZ-store mode when the workspace holds dZ^T (the size fmlp_bwd_workspace_size asks
-  // for); otherwise the dX programs recompute Z and dH (needs ws_need bytes at least)
-  const size_t ws_dz = (f32 || !allow_dz) ? 0 : bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count);
-  const bool dz_mode = ws_dz != 0 && workspace_bytes >= ws_dz && workspace != nullptr && aligned16(workspace);
-  if (!dz_mode && (workspace_bytes < ws_need || (ws_need && (workspace == nullptr || !aligned16(workspace)))))
-    return FMLP_ERR_WORKSPACE;
+  // for); otherwise the dX programs recompute Z and dH
+  BwdPlan plan;
+  if ((rc = plan_bwd(H, B, D, E, f32, allow_dz, dev->sm_count, workspace_bytes,
+                     workspace != nullptr && aligned16(workspace), &plan)))
+    return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (H == 0 || D == 0) return FMLP_OK;
   const size_t esz = elem_bytes(dtype);
@@ -314,15 +335,9 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
   a.x = x, a.w1 = w1;
   a.dx = dx, a.dw1 = dw1, a.dw2 = dw2;
   a.dw_f32 = dwf;
-  if (dz_mode) {
-    const size_t dz = bwd_dz_bytes(H, B, D, E, dev->sm_count);
-    a.dzt = workspace;
-    a.splits = bwd_dz_splits(H, B, D, E, dev->sm_count);
-    a.part = a.splits > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + dz) : nullptr;
-  } else {
-    a.splits = ws_need ? bwd_dw_splits(H, B, D, E, dev->sm_count) : 1;
-    a.part = ws_need ? static_cast<float*>(workspace) : nullptr;
-  }
+  a.splits = plan.splits;
+  a.dzt = plan.dz ? workspace : nullptr;
+  a.part = plan.splits > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + plan.dz_bytes) : nullptr;
   a.sm_count = dev->sm_count;
   a.H = H, a.B = B, a.D = D, a.E = E;
   a.bf16 = bf;
