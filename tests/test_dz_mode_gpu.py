@@ -178,3 +178,23 @@ def test_dz_mode_writes_stay_inside_their_buffers():
     want = F().flashmlp_bwd(x, w1, w2, do, "silu")
     for b, w in zip(bufs, want):
         assert torch.equal(b[G:-G].view_as(w), w)
+
+
+def test_dz_mode_cap_selects_recompute_above_8_gib():
+    # C4 on one GPU needs exactly 8 GiB of dZ^T (the cap: every element offset fits in 32
+    # bits); one more head does not fit, and the library asks for the recompute mode's
+    # workspace instead. Plan queries only, nothing is allocated.
+    from flashmlp_b200 import _lib
+
+    L = _lib.lib()
+    B, D, E = 65536, 128, 2048
+    assert _plan(32, B, D, E, torch.bfloat16) == (1, 2, 3)
+    assert int(L.fmlp_bwd_workspace_size(32, B, D, E, 1)) >= 8 << 30
+    mode, splits, launches = _plan(33, B, D, E, torch.bfloat16)
+    assert mode == 0 and launches == 1 + (splits > 1)
+    assert int(L.fmlp_bwd_workspace_size(33, B, D, E, 1)) == int(L.fmlp_bwd_workspace_size_min(33, B, D, E, 1))
+    # below fmlp_bwd_workspace_size_min the plan (and fmlp_bwd) refuse the call
+    need = int(L.fmlp_bwd_workspace_size_min(4, B, D, E, 1))
+    assert need > 0
+    with pytest.raises(_lib.FlashMLPError):
+        _lib.bwd_plan(4, B, D, E, 1, need - 16)
