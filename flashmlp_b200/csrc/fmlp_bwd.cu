@@ -824,18 +824,19 @@ int bwd_dz_splits(int H, int B, int D, int E, int sm_count) {
   if (D > 128 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 1;
   const long long nB = (B + kRows - 1) / kRows, nE = (E + kBwdEt - 1) / kBwdEt;
   // The launch holds dW programs only, all of the same length, so it runs in whole waves
-  // of sm_count programs: pick S (1..8, at least 2 B tiles per split) minimising
-  // waves * tiles per program * tile time + the fp32 reduce of the partials (S > 1).
+  // of sm_count programs: pick S (1..16, at least 2 B tiles per split) minimising
+  // waves * (tiles per program + 2 for a program's fill and drain) * tile time + the fp32
+  // reduce of the partials (S > 1).
   const int dp = D <= 64 ? 64 : 128;
   const double tile_s = 8.0 * 128 * 128 * dp / (1.2e15 / sm_count);  // 4 products of 128x128xDP
   const double hde = double(H) * D * E;
-  const long long max_s = nB / 2 < 8 ? nB / 2 : 8;
+  const long long max_s = nB / 2 < 16 ? nB / 2 : 16;
   int best = 1;
   double best_t = 0;
   for (long long s = 1; s <= (max_s < 1 ? 1 : max_s); ++s) {
     const long long progs = (long long)H * nE * s;
     const long long waves = (progs + sm_count - 1) / sm_count;
-    double t = double(waves) * double((nB + s - 1) / s) * tile_s;
+    double t = double(waves) * double((nB + s - 1) / s + 2) * tile_s;
     if (s > 1) t += (8.0 * s + 4.0) * hde / 6.0e12 + 5e-6;
     if (s == 1 || t < best_t) best = int(s), best_t = t;
   }
