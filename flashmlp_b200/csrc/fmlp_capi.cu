@@ -107,7 +107,7 @@ struct BwdPlan {
 
 int plan_bwd(int H, int B, int D, int E, bool f32, bool allow_dz, int sm_count, size_t workspace_bytes,
              bool usable, BwdPlan* p) {
-  const size_t need = f32 ? 0 : bwd_workspace_bytes(H, B, D, E, sm_count);
+  const size_t need = f32 ? bwd_workspace_bytes_tf32(H, B, D, E, sm_count) : bwd_workspace_bytes(H, B, D, E, sm_count);
   const size_t ws_dz = (f32 || !allow_dz) ? 0 : bwd_dz_workspace_bytes(H, B, D, E, sm_count);
   p->dz = ws_dz != 0 && workspace_bytes >= ws_dz && usable;
   if (!p->dz && (workspace_bytes < need || (need && !usable))) return FMLP_ERR_WORKSPACE;
@@ -115,7 +115,7 @@ int plan_bwd(int H, int B, int D, int E, bool f32, bool allow_dz, int sm_count, 
     p->splits = bwd_dz_splits(H, B, D, E, sm_count);
     p->dz_bytes = bwd_dz_bytes(H, B, D, E, sm_count);
   } else {
-    p->splits = need ? bwd_dw_splits(H, B, D, E, sm_count) : 1;
+    p->splits = need ? (f32 ? bwd_dw_splits_tf32(H, B, D, E, sm_count) : bwd_dw_splits(H, B, D, E, sm_count)) : 1;
   }
   return FMLP_OK;
 }
@@ -237,10 +237,10 @@ int fmlp_fwd_shared_x(const void* x, const void* w1, const void* w2, void* o, in
 
 size_t fmlp_bwd_workspace_size_min(int H, int B, int D, int E, int dtype) {
   if (check_common(H, B, D, E, dtype) || D % 16 != 0 || D > 256 || E % 8 != 0) return 0;
-  if (dtype == FMLP_DTYPE_F32) return 0;  // the fp32 backward does not split its dW programs
   DeviceInfo* dev = nullptr;
   if (device_info(&dev)) return 0;
-  return bwd_workspace_bytes(H, B, D, E, dev->sm_count);
+  return dtype == FMLP_DTYPE_F32 ? bwd_workspace_bytes_tf32(H, B, D, E, dev->sm_count)
+                                 : bwd_workspace_bytes(H, B, D, E, dev->sm_count);
 }
 
 size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {

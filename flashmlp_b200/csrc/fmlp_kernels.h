@@ -78,6 +78,9 @@ int current_device_status(int* sm_count, uint32_t** status);
 // bytes it needs: 2 * splits * H * D * E * 4 when splits > 1.
 int bwd_dw_splits(int H, int B, int D, int E, int sm_count);
 size_t bwd_workspace_bytes(int H, int B, int D, int E, int sm_count);
+// The same for the fp32 (TF32) backward, whose dW programs walk 32-row B tiles.
+int bwd_dw_splits_tf32(int H, int B, int D, int E, int sm_count);
+size_t bwd_workspace_bytes_tf32(int H, int B, int D, int E, int sm_count);
 
 // dZ-store mode of the 16-bit backward (D <= 256): the dW programs also store dZ^T and
 // a GEMM over E forms dX from it (fmlp_dxgemm.cu). bwd_dz_bytes is the dZ^T workspace

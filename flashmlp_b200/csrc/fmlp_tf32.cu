@@ -335,7 +335,8 @@ template <int DP, int ACT>
 __global__ void __launch_bounds__(576, 1)
     fmlp_bwd_tf32_kernel(const __grid_constant__ Tf32BwdMaps tm, const float* __restrict__ X,
                          const float* __restrict__ W1, float* __restrict__ dX, float* __restrict__ dW1,
-                         float* __restrict__ dW2, int H, int B, int D, int E, uint32_t* status) {
+                         float* __restrict__ dW2, float* __restrict__ part, int splits, int H, int B, int D,
+                         int E, uint32_t* status) {
   using C = BwdTf32Cfg<DP>;
   using St = ActState<float, ACT>;
   constexpr int BM = C::BM, T = C::T;
@@ -351,15 +352,29 @@ __global__ void __launch_bounds__(576, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int nEw = (E + C::EW - 1) / C::EW;  // dW programs per head
-  const bool is_dw = int(blockIdx.x) < H * nEw;
-  int h, idx;
+  const int nEw = (E + C::EW - 1) / C::EW;  // dW programs per head and B range
+  // dW programs: (head, split, E chunk), chunk fastest; with splits > 1 each covers a
+  // contiguous range of the 32-row B tiles and writes fp32 partial sums to `part`
+  // (part[split][0] = dW1 (H,D,E), part[split][1] = dW2 (H,E,D)), added in split order by
+  // fmlp_dw_reduce_f32_kernel
+  const bool is_dw = int(blockIdx.x) < H * nEw * splits;
+  int h, idx, t0 = 0, t1 = 0;
   if (is_dw) {
-    h = blockIdx.x / nEw;
-    idx = blockIdx.x % nEw;  // E chunk
+    h = blockIdx.x / (nEw * splits);
+    const int r = blockIdx.x % (nEw * splits);
+    const int split = r / nEw;
+    idx = r % nEw;  // E chunk
+    const int nTt = (B + T - 1) / T;
+    t0 = int((long long)split * nTt / splits);
+    t1 = int((long long)(split + 1) * nTt / splits);
+    if (part != nullptr) {
+      const size_t n = size_t(H) * D * E;
+      dW1 = part + size_t(split) * 2 * n;
+      dW2 = dW1 + n;
+    }
   } else {
     const int nBx = (B + BM - 1) / BM;
-    const int p = blockIdx.x - H * nEw;
+    const int p = blockIdx.x - H * nEw * splits;
     h = p / nBx;
     idx = p % nBx;  // B tile
   }
@@ -439,7 +454,7 @@ __global__ void __launch_bounds__(576, 1)
   if (is_dw) {
     // ==================================================================== dW program
     const int c = idx;
-    const int nT = (B + T - 1) / T;
+    const int nT = t1 - t0;  // 32-row tiles of this program; tile t of the loops is t0 + t
     uint8_t* sW2 = smem + C::W_OFF_W2;
     constexpr int WS = C::WS;
     // stage s: X_K, X_MN, dO_K, dO_MN
@@ -459,10 +474,10 @@ __global__ void __launch_bounds__(576, 1)
           mbar_arrive_expect_tx(&ring_full[s], C::W_STAGE);
           for (int r = 0; r < DP / kF32Row; ++r) {
             const int off = r * (T * 128);
-            tma_load_3d(tile(s, 0) + off, &tm.x_k, &ring_full[s], kF32Row * r, t * T, h);
-            tma_load_3d(tile(s, 1) + off, &tm.x_mn, &ring_full[s], kF32Row * r, t * T, h);
-            tma_load_3d(tile(s, 2) + off, &tm.do_k, &ring_full[s], kF32Row * r, t * T, h);
-            tma_load_3d(tile(s, 3) + off, &tm.do_mn, &ring_full[s], kF32Row * r, t * T, h);
+            tma_load_3d(tile(s, 0) + off, &tm.x_k, &ring_full[s], kF32Row * r, (t0 + t) * T, h);
+            tma_load_3d(tile(s, 1) + off, &tm.x_mn, &ring_full[s], kF32Row * r, (t0 + t) * T, h);
+            tma_load_3d(tile(s, 2) + off, &tm.do_k, &ring_full[s], kF32Row * r, (t0 + t) * T, h);
+            tma_load_3d(tile(s, 3) + off, &tm.do_mn, &ring_full[s], kF32Row * r, (t0 + t) * T, h);
           }
           ++nl;
         }
@@ -783,6 +798,25 @@ static cudaError_t launch_fwd_tf32_t(const FwdLaunch& a) {
   return cudaGetLastError();
 }
 
+// dW1 / dW2 of split fp32 dW programs: out[i] = sum over s = 0..S-1, in that order, of
+// part[s][which][i] (which = blockIdx.y: 0 = dW1 into o1, 1 = dW2 into o2), four elements
+// per step (H*D*E is a multiple of 4). Deterministic, no atomics.
+__global__ void __launch_bounds__(256)
+    fmlp_dw_reduce_f32_kernel(const float* __restrict__ part, float* __restrict__ o1, float* __restrict__ o2,
+                              long long n4, int splits) {
+  const long long n = n4 * 4;
+  const float4* src = reinterpret_cast<const float4*>(part + blockIdx.y * n);
+  float4* dst = reinterpret_cast<float4*>(blockIdx.y ? o2 : o1);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    float4 acc = __ldcs(src + i);
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 v = __ldcs(src + size_t(sp) * 2 * n4 + i);
+      acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+    }
+    dst[i] = acc;
+  }
+}
+
 template <int DP, int ACT>
 static cudaError_t launch_bwd_tf32_t(const BwdLaunch& a) {
   using C = BwdTf32Cfg<DP>;
@@ -791,7 +825,9 @@ static cudaError_t launch_bwd_tf32_t(const BwdLaunch& a) {
   if (e != cudaSuccess) return e;
   const int nBx = (a.B + kRows - 1) / kRows;
   const int nEw = (a.E + C::EW - 1) / C::EW;
-  const long long grid = (long long)a.H * (nEw + nBx);
+  const int splits = a.splits < 1 ? 1 : a.splits;
+  if (splits > 1 && (a.part == nullptr || splits > (a.B + C::T - 1) / C::T)) return cudaErrorInvalidValue;
+  const long long grid = (long long)a.H * ((long long)nEw * splits + nBx);
   if (grid <= 0 || grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   // dW as fp32 into dw_f32 (dW1 (H,D,E) then dW2 (H,E,D)) when given, else into dw1 / dw2
   float* d1 = a.dw_f32 ? a.dw_f32 : reinterpret_cast<float*>(a.dw1);
@@ -799,7 +835,14 @@ static cudaError_t launch_bwd_tf32_t(const BwdLaunch& a) {
   if (a.tf32_maps == nullptr) return cudaErrorInvalidValue;
   kern<<<unsigned(grid), C::NUM_THREADS, C::SMEM, a.stream>>>(
       *a.tf32_maps, reinterpret_cast<const float*>(a.x), reinterpret_cast<const float*>(a.w1),
-      reinterpret_cast<float*>(a.dx), d1, d2, a.H, a.B, a.D, a.E, a.status);
+      reinterpret_cast<float*>(a.dx), d1, d2, splits > 1 ? a.part : nullptr, splits, a.H, a.B, a.D, a.E, a.status);
+  cudaError_t le = cudaGetLastError();
+  if (le != cudaSuccess || splits == 1) return le;
+  const long long n4 = (long long)a.H * a.D * a.E / 4;  // E % 8 == 0
+  long long blocks = (n4 + 255) / 256;
+  const long long cap = (long long)a.sm_count * 4;
+  if (blocks > cap) blocks = cap;
+  fmlp_dw_reduce_f32_kernel<<<dim3(unsigned(blocks), 2), 256, 0, a.stream>>>(a.part, d1, d2, n4, splits);
   return cudaGetLastError();
 }
 
@@ -829,6 +872,27 @@ cudaError_t launch_fwd_tf32(const FwdLaunch& a) {
     case 128: return launch_fwd_tf32_dp<128>(a);
   }
   return cudaErrorNotSupported;
+}
+
+int bwd_dw_splits_tf32(int H, int B, int D, int E, int sm_count) {
+  if (D > 128 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 1;
+  constexpr int T = 32;
+  const long long nT = (B + T - 1) / T, nBx = (B + kRows - 1) / kRows, nEw = (E + 127) / 128, nEx = (E + T - 1) / T;
+  // Work in units of one 128 x 32 x DP product: a dW program does 4 per 32-row tile, a dX
+  // program 3 per 32-wide E chunk. Split until one dW program is at most 0.8 of an SM's
+  // share of the launch, keeping at least 2 tiles per split and at most 8 splits.
+  const long long work = 4LL * H * nEw * nT + 3LL * H * nBx * nEx;
+  const long long max_s = nT / 2 < 8 ? nT / 2 : 8;
+  for (long long s = 1; s <= max_s; ++s) {
+    const long long lw = 4 * ((nT + s - 1) / s);
+    if (5 * lw * sm_count <= 4 * work) return int(s);
+  }
+  return max_s < 1 ? 1 : int(max_s);
+}
+
+size_t bwd_workspace_bytes_tf32(int H, int B, int D, int E, int sm_count) {
+  const int s = bwd_dw_splits_tf32(H, B, D, E, sm_count);
+  return s > 1 ? size_t(2) * s * size_t(H) * D * E * sizeof(float) : 0;
 }
 
 cudaError_t launch_bwd_tf32(const BwdLaunch& a) {

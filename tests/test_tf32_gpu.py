@@ -80,3 +80,31 @@ def test_tf32_module_matches_pytorch_module():
         assert torch.allclose(g1, pm.w1.grad, atol=2e-2, rtol=2e-2)
         pm.w1.grad = None
         x.grad = None
+
+
+def test_tf32_split_dw_programs():
+    # 4 heads of C4 in fp32 (the per-GPU launch of 8-way head sharding): 64 (head, E chunk)
+    # dW programs for 148 SMs, so they are split over B ranges, their fp32 partials added
+    # in split order by fmlp_dw_reduce_f32_kernel.
+    from flashmlp_b200 import _lib
+
+    H, B, D, E = 4, 65536, 128, 2048
+    dt = torch.float32
+    L = _lib.lib()
+    need = int(L.fmlp_bwd_workspace_size_min(H, B, D, E, _lib.FMLP_DTYPE_F32))
+    mode, splits, launches = _lib.bwd_plan(H, B, D, E, _lib.FMLP_DTYPE_F32, need)
+    assert need > 0 and mode == 0 and splits > 1 and launches == 2
+    assert int(L.fmlp_bwd_workspace_size(H, B, D, E, _lib.FMLP_DTYPE_F32)) == need
+    x, w1, w2, do = make_inputs(H, B, D, E, dt, seed=44)
+    got = F().flashmlp_bwd(x, w1, w2, do, "silu")
+    refs = ref_bwd(x, w1, w2, do, "silu")
+    for i, k in enumerate(("dx", "dw1", "dw2")):
+        assert_close(got[i], *refs[k], dt, "bwd", k)
+    dxf, dwf = F().flashmlp_bwd_dw_f32(x, w1, w2, do, "silu")
+    n1 = H * D * E
+    assert torch.equal(dxf, got[0])
+    assert torch.equal(dwf[:n1].view(H, D, E), got[1]) and torch.equal(dwf[n1:].view(H, E, D), got[2])
+    # a second call repeats every bit
+    again = F().flashmlp_bwd(x, w1, w2, do, "silu")
+    for u, v in zip(got, again):
+        assert torch.equal(u, v)
