@@ -813,10 +813,10 @@ size_t bwd_workspace_bytes(int H, int B, int D, int E, int sm_count) {
   return s > 1 ? size_t(2) * s * size_t(H) * D * E * sizeof(float) : 0;
 }
 
-size_t bwd_dz_bytes(int H, int B, int D, int E, int sm_count) {
-  if (D > 256 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 0;
+size_t bwd_dz_bytes(int H, int B, int D, int E, int sm_count, int elem_bytes) {
+  if (D > (elem_bytes == 4 ? 128 : 256) || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 0;
   const size_t nB = (size_t(B) + kRows - 1) / kRows, nE = (size_t(E) + kBwdEt - 1) / kBwdEt;
-  const size_t bytes = size_t(H) * nE * kBwdEt * nB * kRows * 2;
+  const size_t bytes = size_t(H) * nE * kBwdEt * nB * kRows * elem_bytes;
   return bytes <= kDzCapBytes ? bytes : 0;
 }
 
@@ -843,10 +843,10 @@ int bwd_dz_splits(int H, int B, int D, int E, int sm_count) {
   return best;
 }
 
-size_t bwd_dz_workspace_bytes(int H, int B, int D, int E, int sm_count) {
-  const size_t dz = bwd_dz_bytes(H, B, D, E, sm_count);
+size_t bwd_dz_workspace_bytes(int H, int B, int D, int E, int sm_count, int elem_bytes) {
+  const size_t dz = bwd_dz_bytes(H, B, D, E, sm_count, elem_bytes);
   if (dz == 0) return 0;
-  const int s = bwd_dz_splits(H, B, D, E, sm_count);
+  const int s = elem_bytes == 4 ? bwd_dz_splits_tf32(H, B, D, E, sm_count) : bwd_dz_splits(H, B, D, E, sm_count);
   return dz + (s > 1 ? size_t(2) * s * size_t(H) * D * E * sizeof(float) : 0);
 }
 

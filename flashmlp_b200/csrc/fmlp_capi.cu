@@ -108,12 +108,13 @@ struct BwdPlan {
 int plan_bwd(int H, int B, int D, int E, bool f32, bool allow_dz, int sm_count, size_t workspace_bytes,
              bool usable, BwdPlan* p) {
   const size_t need = f32 ? bwd_workspace_bytes_tf32(H, B, D, E, sm_count) : bwd_workspace_bytes(H, B, D, E, sm_count);
-  const size_t ws_dz = (f32 || !allow_dz) ? 0 : bwd_dz_workspace_bytes(H, B, D, E, sm_count);
+  const int esz = f32 ? 4 : 2;  // dZ is stored in the input dtype (fp32 stays fp32)
+  const size_t ws_dz = allow_dz ? bwd_dz_workspace_bytes(H, B, D, E, sm_count, esz) : 0;
   p->dz = ws_dz != 0 && workspace_bytes >= ws_dz && usable;
   if (!p->dz && (workspace_bytes < need || (need && !usable))) return FMLP_ERR_WORKSPACE;
   if (p->dz) {
-    p->splits = bwd_dz_splits(H, B, D, E, sm_count);
-    p->dz_bytes = bwd_dz_bytes(H, B, D, E, sm_count);
+    p->splits = f32 ? bwd_dz_splits_tf32(H, B, D, E, sm_count) : bwd_dz_splits(H, B, D, E, sm_count);
+    p->dz_bytes = bwd_dz_bytes(H, B, D, E, sm_count, esz);
   } else {
     p->splits = need ? (f32 ? bwd_dw_splits_tf32(H, B, D, E, sm_count) : bwd_dw_splits(H, B, D, E, sm_count)) : 1;
   }
@@ -245,11 +246,10 @@ size_t fmlp_bwd_workspace_size_min(int H, int B, int D, int E, int dtype) {
 
 size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {
   const size_t least = fmlp_bwd_workspace_size_min(H, B, D, E, dtype);
-  if (dtype == FMLP_DTYPE_F32 || D > 256 || check_common(H, B, D, E, dtype) || D % 16 != 0 || E % 8 != 0)
-    return least;
+  if (D > 256 || check_common(H, B, D, E, dtype) || D % 16 != 0 || E % 8 != 0) return least;
   DeviceInfo* dev = nullptr;
   if (device_info(&dev)) return 0;
-  const size_t dz = bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count);
+  const size_t dz = bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count, dtype == FMLP_DTYPE_F32 ? 4 : 2);
   return dz ? dz : least;
 }
 
@@ -324,6 +324,10 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
     if ((rc = encode3d(&tm32.w1_k, w1, dtype, E, D, H, 32, a.dp))) return rc;
     if ((rc = encode3d(&tm32.w1_mn, w1, dtype, E, D, H, 32, a.dp, mn))) return rc;
     if ((rc = encode3d(&tm32.w2_k, w2, dtype, D, E, H, 32, 32))) return rc;
+    if (plan.dz) {  // the dZ workspace (H, nB*128, nE*128) fp32, read K-major by the dX GEMM
+      const uint64_t bp = uint64_t((B + kRows - 1) / kRows) * kRows, ep = uint64_t((E + kBwdEt - 1) / kBwdEt) * kBwdEt;
+      if ((rc = encode3d(&tm32.dz, workspace, dtype, ep, bp, H, 32, kRows))) return rc;
+    }
     a.tf32_maps = &tm32;
   } else {
     if ((rc = encode3d(&a.tm_x, x, dtype, D, B, hx, inner, rows))) return rc;

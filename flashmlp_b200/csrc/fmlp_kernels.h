@@ -29,6 +29,7 @@ struct FwdLaunch {
 // W1 DP rows.
 struct Tf32BwdMaps {
   CUtensorMap x_k, x_mn, do_k, do_mn, w1_k, w1_mn, w2_k;
+  CUtensorMap dz;  // dZ-store mode: dZ workspace {nE*128, nB*128, H} fp32, box {32, 128}
 };
 
 struct BwdLaunch {
@@ -81,16 +82,18 @@ size_t bwd_workspace_bytes(int H, int B, int D, int E, int sm_count);
 // The same for the fp32 (TF32) backward, whose dW programs walk 32-row B tiles.
 int bwd_dw_splits_tf32(int H, int B, int D, int E, int sm_count);
 size_t bwd_workspace_bytes_tf32(int H, int B, int D, int E, int sm_count);
+int bwd_dz_splits_tf32(int H, int B, int D, int E, int sm_count);  // dZ-store mode, fp32
 
-// dZ-store mode of the 16-bit backward (D <= 256): the dW programs also store dZ^T and
-// a GEMM over E forms dX from it (fmlp_dxgemm.cu). bwd_dz_bytes is the dZ^T workspace
-// (0 when the mode does not apply or would need more than kDzCapBytes);
-// bwd_dz_splits the dW split factor of that launch, whose fp32 partials follow the dZ^T
-// region (bwd_dz_workspace_bytes is the total).
+// dZ-store mode of the backward (16-bit inputs with D <= 256, fp32 inputs with D <= 128):
+// the dW programs also store dZ and a GEMM over E forms dX from it (fmlp_dxgemm.cu; fp32:
+// fmlp_tf32.cu). bwd_dz_bytes is the dZ workspace for elements of elem_bytes (0 when the
+// mode does not apply or would need more than kDzCapBytes); bwd_dz_splits the dW split
+// factor of that launch, whose fp32 partials follow the dZ region (bwd_dz_workspace_bytes
+// is the total).
 constexpr size_t kDzCapBytes = size_t(8) << 30;
-size_t bwd_dz_bytes(int H, int B, int D, int E, int sm_count);
+size_t bwd_dz_bytes(int H, int B, int D, int E, int sm_count, int elem_bytes = 2);
 int bwd_dz_splits(int H, int B, int D, int E, int sm_count);
-size_t bwd_dz_workspace_bytes(int H, int B, int D, int E, int sm_count);
+size_t bwd_dz_workspace_bytes(int H, int B, int D, int E, int sm_count, int elem_bytes = 2);
 
 // Body of fmlp_bwd; allow_dz = 0 keeps the recompute mode whatever the workspace size
 // (fmlp_bwd_noalloc).

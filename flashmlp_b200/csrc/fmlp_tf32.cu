@@ -335,8 +335,8 @@ template <int DP, int ACT>
 __global__ void __launch_bounds__(576, 1)
     fmlp_bwd_tf32_kernel(const __grid_constant__ Tf32BwdMaps tm, const float* __restrict__ X,
                          const float* __restrict__ W1, float* __restrict__ dX, float* __restrict__ dW1,
-                         float* __restrict__ dW2, float* __restrict__ part, int splits, int H, int B, int D,
-                         int E, uint32_t* status) {
+                         float* __restrict__ dW2, float* __restrict__ part, float* __restrict__ dzt, int splits,
+                         int H, int B, int D, int E, uint32_t* status) {
   using C = BwdTf32Cfg<DP>;
   using St = ActState<float, ACT>;
   constexpr int BM = C::BM, T = C::T;
@@ -436,13 +436,18 @@ __global__ void __launch_bounds__(576, 1)
     for (int i = 0; i < 8; ++i) v[i] = __float_as_uint(act_forward<float, ACT>(__uint_as_float(v[i]), st[i]));
     if (store_h) tmem_st8(col, v);
   };
-  // Phase 2 over the 8 dH columns at `col`: dZ (fp32) in place.
-  auto phase2 = [&](uint32_t col, const St (&st)[8]) {
+  // Phase 2 over the 8 dH columns at `col`: dZ (fp32) in place and, if `g` is set, also
+  // stored to g[0], g[row], ..., g[7 * row] (the dZ-store workspace, one value per b row).
+  auto phase2 = [&](uint32_t col, const St (&st)[8], float* g, uint32_t row) {
     uint32_t v[8];
     tmem_ld8_sync(col, v);
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = __float_as_uint(act_grad<float, ACT>(__uint_as_float(v[i]), st[i]));
     tmem_st8(col, v);
+    if (g != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) g[i * row] = __uint_as_float(v[i]);
+    }
   };
   auto signal = [&](uint64_t* bar, bool wrote_tmem) {
     if (wrote_tmem) tmem_wait_st();
@@ -573,6 +578,14 @@ __global__ void __launch_bounds__(576, 1)
       }
       const uint32_t zt = tmem + lane_off + C::W_TM_ZT + 8 * j;
       const uint32_t dt = tmem + lane_off + C::W_TM_DHT + 8 * j;
+      // dZ-store mode: dZ (not transposed) in the workspace as (H, nB*128, nE*128) fp32,
+      // e contiguous, the K-major operand fmlp_dx_gemm_tf32_kernel reads by TMA. This
+      // thread (e = 128c + 32q + lane) stores b = 32(t0 + t) + 8j + i, i < 8; for each i the
+      // warp's 32 lanes write 128 contiguous bytes. 32-bit element offsets (the workspace
+      // holds at most 2^31 fp32 values).
+      const uint32_t dz_ld = uint32_t(nEw * C::EW);  // row length of the workspace
+      const uint32_t dz_off = uint32_t(size_t(h) * ((B + BM - 1) / BM) * BM * dz_ld) +
+                              uint32_t(T * t0 + 8 * j) * dz_ld + uint32_t(c * C::EW + q * 32 + lane);
       bool ok = true;
       for (int t = 0; t < nT && ok; ++t) {
         St st[8];
@@ -582,7 +595,7 @@ __global__ void __launch_bounds__(576, 1)
         signal(&a_full[0], true);
         if (!(ok = mbar_wait(&p_full[1], t & 1, ctx))) break;
         tc_fence_after();
-        phase2(dt, st);  // dZ^T in place of dH^T
+        phase2(dt, st, dzt != nullptr ? dzt + (dz_off + uint32_t(t * T) * dz_ld) : nullptr, dz_ld);  // dZ^T in place of dH^T
         signal(&a_full[1], true);
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
@@ -757,7 +770,7 @@ __global__ void __launch_bounds__(576, 1)
         signal(&a_full[0], false);
         if (!(ok = mbar_wait(&p_full[1], c & 1, ctx))) break;
         tc_fence_after();
-        phase2(da, st);  // dZ in place of dH
+        phase2(da, st, nullptr, 0);  // dZ in place of dH
         signal(&a_full[1], true);
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
@@ -798,6 +811,152 @@ static cudaError_t launch_fwd_tf32_t(const FwdLaunch& a) {
   return cudaGetLastError();
 }
 
+// dX of the dZ-store mode for fp32 inputs: dX[h, b, :] = sum over e of dZ[h, b, e] *
+// W1[h, :, e] with TF32 products and fp32 accumulation -- the dX programs' last product on
+// the dZ the dW programs stored (fp32, as the dX programs keep it). One CTA per (128-row B
+// tile, head); warp 0 issues TMA loads, warp 1 the MMAs, warps 2-5 store dX. K steps of
+// 32 e, both operands K-major with the ordinary 128-byte swizzle:
+//   dX(b, d) += dZ(b, e) [smem, box {32 e, 128 b}] @ W1^T(e, d) [smem, box {32 e, DP d}]
+//   kind::tf32 M=128(b) N=DP K=8, four per stage; 3 stages of 32 KB (DP = 128), two CTAs
+//   per SM. HBM-bound: 4*E bytes of dZ per output row.
+template <int DP>
+struct DxGemmTf32Cfg {
+  static constexpr int BM = kRows;
+  static constexpr int KT = 32;
+  static constexpr int A_BYTES = BM * KT * 4;
+  static constexpr int B_BYTES = DP * KT * 4;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int NST = DP == 64 ? 4 : 3;
+  static constexpr int OFF_BAR = NST * STAGE;
+  static constexpr int OFF_MISC = OFF_BAR + (2 * NST + 2) * 8;
+  static constexpr int SMEM = OFF_MISC + 16 + 1024;
+  static constexpr int NUM_THREADS = 192;
+  static_assert(2 * (SMEM + 1024) <= 233472, "two CTAs per SM");
+};
+
+template <int DP>
+__global__ void __launch_bounds__(192)
+    fmlp_dx_gemm_tf32_kernel(const __grid_constant__ CUtensorMap tm_dz, const __grid_constant__ CUtensorMap tm_w1,
+                             float* __restrict__ dX, int B, int D, int E, uint32_t* status) {
+  using C = DxGemmTf32Cfg<DP>;
+  constexpr int BM = C::BM;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* empty = full + C::NST;
+  uint64_t* acc_full = empty + C::NST;
+  uint64_t* done_bar = acc_full + 1;
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile uint32_t* abort_flag = misc + 1;
+  const WaitCtx ctx{abort_flag, status};
+  const WaitCtx drain{misc + 2, status};  // misc[2] stays 0: drains never abort early
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bt = blockIdx.x;
+  const int h = blockIdx.y;
+  const int nK = (E + C::KT - 1) / C::KT;
+  if (threadIdx.x == 0) {
+    misc[1] = 0;
+    misc[2] = 0;
+    for (int i = 0; i < C::NST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_dz);
+    tma_prefetch_desc(&tm_w1);
+  }
+  if (warp == 1) {
+    tmem_alloc(misc, DP);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[0];
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t n = 0;
+      for (int k = 0; k < nK; ++k) {
+        const int s = k % C::NST;
+        if (!mbar_wait(&empty[s], ((k / C::NST) & 1) ^ 1, ctx)) break;
+        uint8_t* st = smem + s * C::STAGE;
+        mbar_arrive_expect_tx(&full[s], C::STAGE);
+        tma_load_3d(st, &tm_dz, &full[s], k * C::KT, bt * BM, h);
+        tma_load_3d(st + C::A_BYTES, &tm_w1, &full[s], k * C::KT, 0, h);
+        ++n;
+      }
+      for (uint32_t k = 0; k < uint32_t(C::NST); ++k)
+        if (n > k) mbar_wait(&full[(n - 1 - k) % C::NST], ((n - 1 - k) / C::NST) & 1, drain);
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc = make_idesc_tf32(128, DP, false, false);  // A K, B K
+    bool ok = true;
+    for (int k = 0; k < nK && ok; ++k) {
+      const int s = k % C::NST;
+      if (!(ok = warp_wait(&full[s], (k / C::NST) & 1, ctx))) break;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t st = smem_u32(smem + s * C::STAGE);
+        const uint64_t ad = make_sdesc_sw128(st, 16, 1024);
+        const uint64_t bd = make_sdesc_sw128(st + C::A_BYTES, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < C::KT / 8; ++kk)  // K = 8 tf32 = 32 bytes per MMA
+          mma_ss_tf32(tmem, sdesc_add(ad, kk * 32), sdesc_add(bd, kk * 32), idesc, (k > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&empty[s]);
+      }
+      __syncwarp();
+    }
+    if (ok) {
+      if (elect_one()) mma_commit(acc_full);
+      __syncwarp();
+    }
+    if (elect_one()) mma_commit(done_bar);
+    __syncwarp();
+    warp_wait(done_bar, 0, drain);
+  } else {
+    const int q = warp & 3;
+    if (mbar_wait(acc_full, 0, ctx)) {
+      tc_fence_after();
+      const int row = bt * BM + q * 32 + lane;
+      float* xrow = dX + (size_t(h) * B + row) * D;
+      const uint32_t ta = tmem + (uint32_t(q * 32) << 16);
+#pragma unroll
+      for (int u = 0; u < DP / 16; ++u) {
+        uint32_t v[16];
+        tmem_ld16_sync(ta + 16 * u, v);
+        const int cc = 16 * u;
+        if (row < B && cc < D) {  // D % 16 == 0
+          float4* dst = reinterpret_cast<float4*>(xrow + cc);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]), __uint_as_float(v[4 * i + 2]),
+                                 __uint_as_float(v[4 * i + 3]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, DP);
+}
+
+template <int DP>
+static cudaError_t launch_dx_gemm_tf32(const BwdLaunch& a) {
+  using C = DxGemmTf32Cfg<DP>;
+  auto kern = fmlp_dx_gemm_tf32_kernel<DP>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const long long nB = (a.B + kRows - 1) / kRows;
+  if (nB <= 0 || nB > 0x7FFFFFFFLL || a.H <= 0 || a.H > 65535 || a.tf32_maps == nullptr) return cudaErrorInvalidValue;
+  kern<<<dim3(unsigned(nB), unsigned(a.H)), C::NUM_THREADS, C::SMEM, a.stream>>>(
+      a.tf32_maps->dz, a.tf32_maps->w1_k, reinterpret_cast<float*>(a.dx), a.B, a.D, a.E, a.status);
+  return cudaGetLastError();
+}
+
 // dW1 / dW2 of split fp32 dW programs: out[i] = sum over s = 0..S-1, in that order, of
 // part[s][which][i] (which = blockIdx.y: 0 = dW1 into o1, 1 = dW2 into o2), four elements
 // per step (H*D*E is a multiple of 4). Deterministic, no atomics.
@@ -827,7 +986,9 @@ static cudaError_t launch_bwd_tf32_t(const BwdLaunch& a) {
   const int nEw = (a.E + C::EW - 1) / C::EW;
   const int splits = a.splits < 1 ? 1 : a.splits;
   if (splits > 1 && (a.part == nullptr || splits > (a.B + C::T - 1) / C::T)) return cudaErrorInvalidValue;
-  const long long grid = (long long)a.H * ((long long)nEw * splits + nBx);
+  // dZ-store mode: dW programs only (they store dZ), then fmlp_dx_gemm_tf32_kernel
+  const bool dz = a.dzt != nullptr;
+  const long long grid = (long long)a.H * ((long long)nEw * splits + (dz ? 0 : nBx));
   if (grid <= 0 || grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   // dW as fp32 into dw_f32 (dW1 (H,D,E) then dW2 (H,E,D)) when given, else into dw1 / dw2
   float* d1 = a.dw_f32 ? a.dw_f32 : reinterpret_cast<float*>(a.dw1);
@@ -835,8 +996,10 @@ static cudaError_t launch_bwd_tf32_t(const BwdLaunch& a) {
   if (a.tf32_maps == nullptr) return cudaErrorInvalidValue;
   kern<<<unsigned(grid), C::NUM_THREADS, C::SMEM, a.stream>>>(
       *a.tf32_maps, reinterpret_cast<const float*>(a.x), reinterpret_cast<const float*>(a.w1),
-      reinterpret_cast<float*>(a.dx), d1, d2, splits > 1 ? a.part : nullptr, splits, a.H, a.B, a.D, a.E, a.status);
+      reinterpret_cast<float*>(a.dx), d1, d2, splits > 1 ? a.part : nullptr, reinterpret_cast<float*>(a.dzt), splits,
+      a.H, a.B, a.D, a.E, a.status);
   cudaError_t le = cudaGetLastError();
+  if (le == cudaSuccess && dz) le = launch_dx_gemm_tf32<DP>(a);
   if (le != cudaSuccess || splits == 1) return le;
   const long long n4 = (long long)a.H * a.D * a.E / 4;  // E % 8 == 0
   long long blocks = (n4 + 255) / 256;
@@ -888,6 +1051,28 @@ int bwd_dw_splits_tf32(int H, int B, int D, int E, int sm_count) {
     if (5 * lw * sm_count <= 4 * work) return int(s);
   }
   return max_s < 1 ? 1 : int(max_s);
+}
+
+int bwd_dz_splits_tf32(int H, int B, int D, int E, int sm_count) {
+  if (D > 128 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 1;
+  constexpr int T = 32;
+  const long long nT = (B + T - 1) / T, nEw = (E + 127) / 128;
+  // dZ-store mode: the launch holds dW programs only, all of the same length, so it runs
+  // in whole waves (as bwd_dz_splits): S in 1..16 minimising waves * (tiles per program +
+  // 2) * tile time + the fp32 reduce of the partials.
+  const int dp = D <= 64 ? 64 : 128;
+  const double tile_s = 8.0 * 128 * T * dp / (0.5e15 / sm_count);  // 4 TF32 products of 128x32xDP
+  const double hde = double(H) * D * E;
+  const long long max_s = nT / 2 < 16 ? nT / 2 : 16;
+  int best = 1;
+  double best_t = 0;
+  for (long long s = 1; s <= (max_s < 1 ? 1 : max_s); ++s) {
+    const long long waves = (H * nEw * s + sm_count - 1) / sm_count;
+    double t = double(waves) * double((nT + s - 1) / s + 2) * tile_s;
+    if (s > 1) t += (8.0 * s + 8.0) * hde / 6.0e12 + 5e-6;
+    if (s == 1 || t < best_t) best = int(s), best_t = t;
+  }
+  return best;
 }
 
 size_t bwd_workspace_bytes_tf32(int H, int B, int D, int E, int sm_count) {

@@ -1,4 +1,5 @@
-"""The dZ-store mode of the unified backward (16-bit inputs, D <= 256).
+"""The dZ-store mode of the unified backward (16-bit inputs with D <= 256, fp32 inputs with
+D <= 128).
 
 With the workspace fmlp_bwd_workspace_size asks for, the dW programs also store their
 rounded dZ^T tiles and dX is a GEMM over E of those tiles (fmlp_dx_gemm_kernel) instead of
@@ -43,7 +44,8 @@ def F():
 
 def _code(dt):
     from flashmlp_b200 import _lib
-    return _lib.FMLP_DTYPE_BF16 if dt == torch.bfloat16 else _lib.FMLP_DTYPE_F16
+    return {torch.bfloat16: _lib.FMLP_DTYPE_BF16, torch.float16: _lib.FMLP_DTYPE_F16,
+            torch.float32: _lib.FMLP_DTYPE_F32}[dt]
 
 
 def _plan(H, B, D, E, dt, low_memory=False):
@@ -198,3 +200,28 @@ def test_dz_mode_cap_selects_recompute_above_8_gib():
     assert need > 0
     with pytest.raises(_lib.FlashMLPError):
         _lib.bwd_plan(4, B, D, E, 1, need - 16)
+
+
+@pytest.mark.parametrize("shape", [(2, 300, 64, 136), (3, 1000, 128, 264), (4, 65536, 128, 2048)])
+def test_dz_mode_fp32_tf32(shape):
+    # fp32 inputs: the TF32 dW programs (split over B ranges when few) store dZ (fp32,
+    # (H, B, E) with e contiguous) and a TF32 GEMM forms dX from it.
+    H, B, D, E = shape
+    dt = torch.float32
+    fast, slow = _plan(H, B, D, E, dt), _plan(H, B, D, E, dt, low_memory=True)
+    assert fast[0] == 1 and slow[0] == 0
+    x, w1, w2, do = make_inputs(H, B, D, E, dt, seed=B + D)
+    acts = ACTS if B < 10000 else ["silu"]
+    for act in acts:
+        a = F().flashmlp_bwd(x, w1, w2, do, act)
+        with F().low_memory_backward():
+            b = F().flashmlp_bwd(x, w1, w2, do, act)
+        refs = ref_bwd(x, w1, w2, do, act)
+        for i, k in enumerate(("dx", "dw1", "dw2")):
+            assert_close(a[i], *refs[k], dt, "bwd", f"{shape} {act} {k}")
+            assert_close(a[i], b[i], refs[k][1], dt, "bwd", f"{shape} {act} {k} dz vs recompute")
+        if fast[1] == slow[1]:
+            assert torch.equal(a[1], b[1]) and torch.equal(a[2], b[2])
+        c = F().flashmlp_bwd(x, w1, w2, do, act)
+        for u, v in zip(a, c):
+            assert torch.equal(u, v)
