@@ -7,7 +7,7 @@ matters for the small BASELINE configs whose kernels take tens of microseconds. 
 only enqueues kernels and memsets on the caller's stream, so the captured step must give,
 on new data copied into the captured input buffers, exactly the results of eager calls:
 compared bit for bit here, in the dZ-store mode (split and unsplit dW programs), the
-recompute mode and the D = 256 kernel.
+recompute mode, the D = 256 kernel and the fp32 (TF32) kernels.
 """
 import pytest
 import torch
@@ -32,6 +32,7 @@ def _cuda():
     ((2, 4096, 128, 256), torch.bfloat16, "sigmoid", False),  # split dW programs + reduce
     ((3, 1000, 96, 200), torch.bfloat16, "leaky_relu", True),  # recompute mode
     ((2, 700, 256, 264), torch.float16, "silu", False),       # D = 256
+    ((2, 4096, 128, 512), torch.float32, "silu", False),      # fp32: TF32 kernels, split dW + dZ-store
 ])
 def test_captured_step_matches_eager(shape, dtype, act, low_memory):
     import contextlib
