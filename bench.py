@@ -6,11 +6,25 @@ For N > 1 launch one process per GPU with torch.distributed.run; heads are split
 ranks (32/N per GPU, no communication) and the time is the max over ranks. One step is
 one forward + one unified backward over the rank's heads with the batch B=65536, D=128,
 E=2048, bf16, silu. Metric: algorithmic TFLOP/s of fwd+bwd (12*H*B*D*E per step) for
-the whole job. Rank 0 prints one JSON line.
+the whole job. Rank 0 prints one JSON line. Around the timed C4 region, and outside it:
+  * parity: before timing, every rank checks head 0 of its shard (forward and backward
+    of the full-shard launch) against an fp32 PyTorch reference on its own GPU;
+  * the recompute-mode backward (low_memory_backward) timed alone, and the peak device
+    memory of a fwd+bwd in both backward modes (measured as the reference's example.py
+    does: max_memory_allocated above the resident inputs);
+  * e2e: the same step from pinned host memory through flashmlp_b200.host.HostPipeline,
+    plus the bare host-link copy rate of the same bytes on the same streams;
+  * c5: BASELINE config 5 (batch-sharded training step, H=8, B=131072 split over the N
+    ranks, D=256, E=1024, fp16 sigmoid) at the same N, with the fused NVLink all-reduce
+    + SGD and with NCCL all-reduce + fmlp_sgd_update, each checked (replicas bit-identical,
+    update equal to the fixed-order sum of the ranks' partial gradients).
 
---impl reference times the reference's PyTorch path (flashmlp_torch_fwd/bwd, restated in
-numpy fp32 by the test oracle, since the reference itself does not travel) on the host
-cores with all threads, on a bounded sample of the same workload, on rank 0 only.
+--impl reference times the reference's own PyTorch path (flashmlp_torch_fwd/bwd,
+flashmlp.py:671-723) on the host cores with all threads, on a bounded sample of the same
+workload, on rank 0 only; the unmodified reference is loaded from baseline/_ref (the
+oracle's numpy restatement stands in when it is absent). At N = 1 it also times the
+reference's Triton kernels (flashmlp_fwd / flashmlp_bwd, flashmlp.py:428-538) on the GPU
+at the full C4 shape (key triton_b200).
 """
 from __future__ import annotations
 
@@ -31,9 +45,11 @@ sys.path.insert(0, str(ROOT))
 WORKLOAD = dict(H=32, B=65536, D=128, E=2048, activation="silu", dtype="bf16")
 WORKLOAD_NAME = "C4 head-sharded fwd+bwd H=32 B=65536 D=128 E=2048 bf16 silu"
 METRIC = "fused MLP fwd+bwd TFLOP/s (algorithmic 12*H*B*D*E per step)"
-FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "sm_max_mhz": 1965.0}
 SPEC_BF16_TFLOPS = 2250.0
 CPU_SAMPLE_ROWS = 8192  # rows of one head per CPU step (about 26 GFLOP of fwd+bwd)
+C5 = dict(H=8, B=131072, D=256, E=1024, activation="sigmoid", dtype="f16")
+C5_NAME = "C5 batch-sharded training step H=8 B=131072 D=256 E=1024 fp16 sigmoid"
 
 
 def load_peaks():
@@ -47,25 +63,46 @@ def load_peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
-def cpu_threads():
-    try:
-        from threadpoolctl import threadpool_info
+def select_peak(clocks, peaks, src):
+    """The bf16 peak that applies to a run whose SM clocks were sampled: the burst figure
+    (cuBLAS timed alone, at max clock) when the median SM clock under load sat at the
+    maximum, otherwise the burst figure scaled by median / max clock."""
+    burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    mx = (clocks or {}).get("sm_max_mhz") or peaks.get("sm_max_mhz") or FALLBACK_PEAKS["sm_max_mhz"]
+    med = (clocks or {}).get("sm_mhz")
+    if not med:
+        return burst, f"{src} bf16_tflops (burst; no clock samples)"
+    if med >= 0.98 * mx:
+        return burst, f"{src} bf16_tflops (burst): median SM clock under load {med:.0f} MHz = max {mx:.0f} MHz"
+    return burst * med / mx, (f"{src} bf16_tflops (burst) x median/max SM clock ({med:.0f}/{mx:.0f} MHz): the run "
+                              "sat below max clock")
 
-        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
-        if n:
-            return max(n)
+
+def set_host_threads():
+    """All host cores for the CPU legs, whatever OMP_NUM_THREADS torchrun exported."""
+    n = os.cpu_count() or 1
+    try:
+        import torch
+
+        torch.set_num_threads(n)
     except Exception:
         pass
-    return os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(n)
+    except Exception:
+        pass
+    return n
 
 
-def cpu_reference_step(inputs):
-    """One fwd+bwd of the reference's PyTorch path (flashmlp.py:671-723) on the CPU."""
-    from oracle import flashmlp_oracle as orc
+def cpu_threads():
+    try:
+        import torch
 
-    x, w1, w2, do = inputs
-    orc.fwd_fp32(x, w1, w2, WORKLOAD["activation"])
-    orc.bwd_fp32(x, w1, w2, do, WORKLOAD["activation"])
+        return torch.get_num_threads()
+    except Exception:
+        return os.cpu_count() or 1
 
 
 def cpu_sample_inputs(rows):
@@ -74,13 +111,46 @@ def cpu_sample_inputs(rows):
     return orc.make_inputs(1, rows, WORKLOAD["D"], WORKLOAD["E"], WORKLOAD["dtype"], seed=0)
 
 
+def cpu_reference_stepper(rows):
+    """(step function, kind, description) for one fwd+bwd of the reference's PyTorch path
+    (flashmlp.py:671-723) on the host: the unmodified reference from baseline/_ref when it
+    is installed, else the oracle's numpy restatement of the same functions."""
+    from oracle.reference_loader import load_reference
+
+    act = WORKLOAD["activation"]
+    inputs = cpu_sample_inputs(rows)
+    ref = None
+    try:
+        ref = load_reference()
+    except Exception:
+        ref = None
+    if ref is not None:
+        import torch
+
+        x, w1, w2, do = (torch.from_numpy(a) for a in inputs)
+
+        def step():
+            ref.flashmlp_torch_fwd(x, w1, w2, act)
+            ref.flashmlp_torch_bwd(x, w1, w2, do, act)
+
+        return step, "reference", "the reference's flashmlp_torch_fwd + flashmlp_torch_bwd in fp32 (torch CPU)"
+    from oracle import flashmlp_oracle as orc
+
+    def step():
+        orc.fwd_fp32(*inputs[:3], act)
+        orc.bwd_fp32(*inputs, act)
+
+    return step, "port", "numpy fp32 restatement of flashmlp_torch_fwd/bwd (reference not installed)"
+
+
 def measure_cpu_baseline(min_seconds=10.0, max_seconds=30.0):
-    inputs = cpu_sample_inputs(CPU_SAMPLE_ROWS)
+    set_host_threads()
+    step, kind, what = cpu_reference_stepper(CPU_SAMPLE_ROWS)
     flops = 12.0 * CPU_SAMPLE_ROWS * WORKLOAD["D"] * WORKLOAD["E"]
-    cpu_reference_step(inputs)  # warm-up
+    step()  # warm-up
     n, t0 = 0, time.perf_counter()
     while True:
-        cpu_reference_step(inputs)
+        step()
         n += 1
         el = time.perf_counter() - t0
         if el >= min_seconds or (el >= max_seconds / 2 and n >= 1):
@@ -89,9 +159,8 @@ def measure_cpu_baseline(min_seconds=10.0, max_seconds=30.0):
         "value": round(flops * n / el / 1e12, 4),
         "unit": "TFLOP/s",
         "cores": cpu_threads(),
-        "kind": "port",
-        "sample": f"{n} x fwd+bwd of 1 head x {CPU_SAMPLE_ROWS} rows of {WORKLOAD_NAME} "
-                  f"(numpy fp32 restatement of flashmlp_torch_fwd/bwd), {el:.1f} s",
+        "kind": kind,
+        "sample": f"{n} x fwd+bwd of 1 head x {CPU_SAMPLE_ROWS} rows of {WORKLOAD_NAME} ({what}), {el:.1f} s",
     }
 
 
@@ -147,21 +216,77 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def run_reference(args, rank):
+# ----------------------------------------------------------------------------- reference arm
+def time_reference_triton(steps, warmup):
+    """The reference's Triton wrappers (flashmlp.py:428-538, autotuned on first call) on
+    cuda:0 at the full C4 shape, CUDA events on torch's current stream (the stream Triton
+    launches on), plus their peak memory as the reference's example.py measures it."""
+    import torch
+
+    from oracle.reference_loader import load_reference
+
+    ref = load_reference()
+    if ref is None or not torch.cuda.is_available():
+        return {"unavailable": "reference not installed in baseline/_ref" if ref is None else "no CUDA device"}
+    H, B, D, E = (WORKLOAD[k] for k in "HBDE")
+    act = WORKLOAD["activation"]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(1000)
+    x = torch.randn(H, B, D, device=dev, generator=g).to(torch.bfloat16)
+    w1 = (torch.randn(H, D, E, device=dev, generator=g) / D ** 0.5).to(torch.bfloat16)
+    w2 = (torch.randn(H, E, D, device=dev, generator=g) / E ** 0.5).to(torch.bfloat16)
+    do = torch.randn(H, B, D, device=dev, generator=g).to(torch.bfloat16)
+    t0 = time.perf_counter()
+    ref.flashmlp_fwd(x, w1, w2, act)
+    ref.flashmlp_bwd(x, w1, w2, do, act)
+    torch.cuda.synchronize()
+    tune_s = time.perf_counter() - t0
+    for _ in range(max(0, warmup - 1)):
+        ref.flashmlp_fwd(x, w1, w2, act)
+        ref.flashmlp_bwd(x, w1, w2, do, act)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3 * steps)]
+    for i in range(steps):
+        ev[3 * i].record()
+        ref.flashmlp_fwd(x, w1, w2, act)
+        ev[3 * i + 1].record()
+        ref.flashmlp_bwd(x, w1, w2, do, act)
+        ev[3 * i + 2].record()
+    torch.cuda.synchronize()
+    fwd = statistics.mean(ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(steps))
+    bwd = statistics.mean(ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(steps))
+    hbde = float(H) * B * D * E
+    torch.cuda.reset_peak_memory_stats(dev)
+    before = torch.cuda.memory_allocated(dev)
+    ref.flashmlp_fwd(x, w1, w2, act)
+    ref.flashmlp_bwd(x, w1, w2, do, act)
+    torch.cuda.synchronize()
+    peak = torch.cuda.max_memory_allocated(dev) - before
+    return {
+        "config": WORKLOAD_NAME, "steps": steps, "autotune_and_compile_s": round(tune_s, 1),
+        "fwd_ms": round(fwd, 4), "bwd_ms": round(bwd, 4), "step_ms": round(fwd + bwd, 4),
+        "fwd_tflops": round(4 * hbde / fwd / 1e9, 2), "bwd_tflops": round(8 * hbde / bwd / 1e9, 2),
+        "tflops": round(12 * hbde / (fwd + bwd) / 1e9, 2),
+        "peak_mem_above_inputs_bytes": int(peak),
+        "timing": "CUDA events on torch's current stream, mean over steps, after autotune and warm-up",
+    }
+
+
+def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    inputs = cpu_sample_inputs(CPU_SAMPLE_ROWS)
+    cores = set_host_threads()
+    step, kind, what = cpu_reference_stepper(CPU_SAMPLE_ROWS)
     flops = 12.0 * CPU_SAMPLE_ROWS * WORKLOAD["D"] * WORKLOAD["E"]
     for _ in range(args.warmup):
-        cpu_reference_step(inputs)
+        step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        cpu_reference_step(inputs)
+        step()
     el = time.perf_counter() - t0
     value = flops * args.steps / el / 1e12
-    sample = (f"each step: fwd+bwd of 1 head x {CPU_SAMPLE_ROWS} rows of {WORKLOAD_NAME}, "
-              f"numpy fp32 restatement of flashmlp_torch_fwd/bwd (the reference is Python and "
-              f"does not travel to the GPU box)")
+    sample = f"each step: fwd+bwd of 1 head x {CPU_SAMPLE_ROWS} rows of {WORKLOAD_NAME}, {what}"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -169,13 +294,107 @@ def run_reference(args, rank):
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOAD_NAME, "sample_rows": CPU_SAMPLE_ROWS, "heads": 1,
                    "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cpu_threads(),
-                         "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores,
+                         "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    if world == 1 and not args.no_triton:
+        try:
+            line["triton_b200"] = time_reference_triton(args.steps, args.warmup)
+        except Exception as e:  # reported, not fatal: the line's value is the CPU path
+            line["triton_b200"] = {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ----------------------------------------------------------------------------- our arm
+def _tests_helpers():
+    sys.path.insert(0, str(ROOT / "tests"))
+    import _refcheck
+
+    return _refcheck
+
+
+def check_head0(F, x, w1, w2, do, act, o, dx, dw1, dw2):
+    """Head 0 of this rank's full-shard results against the fp32 PyTorch reference with the
+    kernels' rounding points: elementwise README tolerance + dot-product bound and the
+    norm-wise bound. Returns (ok, worst norm-wise relative error, message)."""
+    import torch
+
+    rc = _tests_helpers()
+    sl = slice(0, 1)
+    worst, msg = 0.0, ""
+    try:
+        r, bnd = rc.ref_fwd(x[sl], w1[sl], w2[sl], act)
+        rc.assert_close(o[sl], r, bnd, x.dtype, "fwd", "o")
+        worst = max(worst, max(rc.norm_rel_errors(o[sl], r)))
+        del r, bnd
+        refs = rc.ref_bwd(x[sl], w1[sl], w2[sl], do[sl], act)
+        for k, v in (("dx", dx), ("dw1", dw1), ("dw2", dw2)):
+            rc.assert_close(v[sl], *refs[k], x.dtype, "bwd", k)
+            worst = max(worst, max(rc.norm_rel_errors(v[sl], refs[k][0])))
+        del refs
+        ok = True
+    except AssertionError as e:
+        ok, msg = False, str(e)[:300]
+    torch.cuda.empty_cache()
+    return ok, worst, msg
+
+
+def numa_bind(dev):
+    """Binds this process to the CPUs of its GPU's NUMA node when the host has more than
+    one node (pinned buffers allocated afterwards are then node-local). Returns a record."""
+    import torch
+
+    nodes = sorted(p.name for p in Path("/sys/devices/system/node").glob("node[0-9]*"))
+    rec = {"nodes": len(nodes), "gpu_node": None, "bound": False}
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        node = int(Path(f"/sys/bus/pci/devices/{bus}/numa_node").read_text().strip())
+        rec["gpu_node"] = node
+        if len(nodes) > 1 and node >= 0:
+            cpus = Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip()
+            sel = set()
+            for part in cpus.split(","):
+                a, _, b = part.partition("-")
+                sel.update(range(int(a), int(b or a) + 1))
+            os.sched_setaffinity(0, sel)
+            rec["bound"] = True
+    except Exception as e:
+        rec["error"] = f"{type(e).__name__}: {e}"[:120]
+    return rec
+
+
+def copy_only_rates(dev, host_in, dev_in, dev_out, host_out, reps=3):
+    """Host-link rate of the step's bytes alone: the same pinned buffers, H2D and D2H
+    copies running at once on two streams (one cudaMemcpyAsync per tensor), no kernels.
+    Returns (h2d GB/s, d2h GB/s)."""
+    import torch
+
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    bi = sum(t.numel() * t.element_size() for t in host_in)
+    bo = sum(t.numel() * t.element_size() for t in host_out)
+    best_in, best_out = 0.0, 0.0
+    for _ in range(reps):
+        torch.cuda.synchronize(dev)
+        ei = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        eo = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        with torch.cuda.stream(s_in):
+            ei[0].record(s_in)
+            for d, h in zip(dev_in, host_in):
+                d.copy_(h, non_blocking=True)
+            ei[1].record(s_in)
+        with torch.cuda.stream(s_out):
+            eo[0].record(s_out)
+            for h, d in zip(host_out, dev_out):
+                h.copy_(d, non_blocking=True)
+            eo[1].record(s_out)
+        torch.cuda.synchronize(dev)
+        best_in = max(best_in, bi / (ei[0].elapsed_time(ei[1]) / 1e3) / 1e9)
+        best_out = max(best_out, bo / (eo[0].elapsed_time(eo[1]) / 1e3) / 1e9)
+    return best_in, best_out
 
 
 def run_ours(args, rank, world, local_rank):
@@ -187,6 +406,7 @@ def run_ours(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    numa = numa_bind(dev)
     if world > 1:
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                 timeout=datetime.timedelta(seconds=120))
@@ -206,9 +426,34 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
+    def max_over_ranks(vals):
+        t = torch.tensor(vals, device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t.tolist()]
+
+    def gather(vals):
+        t = torch.tensor(vals, device=dev, dtype=torch.float64)
+        if world == 1:
+            return [t.tolist()]
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        return [p.tolist() for p in parts]
+
     for _ in range(args.warmup):
-        F.flashmlp_fwd(x, w1, w2, act)
-        F.flashmlp_bwd(x, w1, w2, do, act)
+        o = F.flashmlp_fwd(x, w1, w2, act)
+        dx, dw1, dw2 = F.flashmlp_bwd(x, w1, w2, do, act)
+    # ---- parity of this rank's shard (head 0 of the full-shard launch) before timing
+    ok, worst, msg = check_head0(F, x, w1, w2, do, act, o, dx, dw1, dw2)
+    del o, dx, dw1, dw2
+    par = gather([1.0 if ok else 0.0, worst])
+    parity = {"ranks_ok": int(sum(p[0] for p in par)), "ranks": world,
+              "max_norm_rel_err": float(f"{max(p[1] for p in par):.3e}"),
+              "checked": "head 0 of every rank's shard: O, dX, dW1, dW2 of the timed launch vs fp32 PyTorch with "
+                         "the kernels' rounding points (README atol/rtol + dot bound per element, and "
+                         "||a-r||_F <= 5e-3 ||r||_F)"}
+    if not ok:
+        parity["rank_error"] = msg
     barrier()
 
     n = args.steps
@@ -229,16 +474,50 @@ def run_ours(args, rank, world, local_rank):
     total_ms = ev[0].elapsed_time(ev[3 * n - 1])
     fwd_ms = [ev[3 * i].elapsed_time(ev[3 * i + 1]) for i in range(n)]
     bwd_ms = [ev[3 * i + 1].elapsed_time(ev[3 * i + 2]) for i in range(n)]
-    t = torch.tensor([total_ms, statistics.mean(fwd_ms), statistics.mean(bwd_ms)], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, fwd_avg, bwd_avg = (float(v) for v in t.tolist())
+    total_ms, fwd_avg, bwd_avg = max_over_ranks([total_ms, statistics.mean(fwd_ms), statistics.mean(bwd_ms)])
     status = F._lib.lib().fmlp_device_status(1)
     # fmlp_fwd_pair_kernel + the backward's launches: fmlp_bwd_kernel, fmlp_dx_gemm_kernel in
     # the dZ-store mode, fmlp_dw_reduce_kernel when the dW programs are split
     bwd_ws = int(F._lib.lib().fmlp_bwd_workspace_size(Hl, B, D, E, 1))
     bwd_mode, bwd_splits, bwd_launches = F._lib.bwd_plan(Hl, B, D, E, 1, bwd_ws)
     launches_per_step = 1 + bwd_launches
+
+    # ---- the recompute-mode backward (the PID-split kernel, low_memory_backward), timed alone
+    with F.low_memory_backward():
+        rmode, rsplits, rlaunch = F._lib.bwd_plan(Hl, B, D, E, 1, int(F._lib.lib().fmlp_bwd_workspace_size_min(
+            Hl, B, D, E, 1)))
+        for _ in range(2):
+            F.flashmlp_bwd(x, w1, w2, do, act)
+        barrier()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for _ in range(n):
+            F.flashmlp_bwd(x, w1, w2, do, act)
+        r1.record()
+        barrier()
+    (rec_ms,) = max_over_ranks([r0.elapsed_time(r1) / n])
+
+    # ---- peak device memory of one fwd+bwd, as the reference's example.py measures it
+    # (max_memory_allocated above what is allocated before the step: the inputs)
+    def peak_of(ctx):
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats(dev)
+        before = torch.cuda.memory_allocated(dev)
+        with ctx:
+            o_ = F.flashmlp_fwd(x, w1, w2, act)
+            r_ = F.flashmlp_bwd(x, w1, w2, do, act)
+        torch.cuda.synchronize()
+        pk = torch.cuda.max_memory_allocated(dev) - before
+        del o_, r_
+        return pk
+
+    import contextlib
+
+    peak_dz = peak_of(contextlib.nullcontext())
+    peak_rec = peak_of(F.low_memory_backward())
+    inputs_bytes = sum(t.numel() * t.element_size() for t in (x, w1, w2, do))
+    peaks_mem = max_over_ranks([peak_dz, peak_rec])
 
     # ---- e2e through the public API with host buffers (pinned), copies inside the timed region
     n_e2e = max(1, min(n, 5))
@@ -264,14 +543,25 @@ def run_ours(args, rank, world, local_rank):
         e2e_step()
     e1.record()
     barrier()
-    te = torch.tensor([e0.elapsed_time(e1)], device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item())
+    (e2e_ms,) = max_over_ranks([e0.elapsed_time(e1)])
+    # the host link alone, all ranks at once (the step's bytes, same pinned buffers)
+    dev_out = [torch.empty_like(t, device=dev) for t in (hx, hx, hw1, hw2)]
+    barrier()
+    cin, cout = copy_only_rates(dev, (hx, hw1, hw2, hdo), (x, w1, w2, do), dev_out, (ho, hdx, hdw1, hdw2))
+    rates = gather([cin, cout])
+    del dev_out, pipe
+
+    # ---- C5 at the same N (batch-sharded training step)
+    del x, w1, w2, do
+    torch.cuda.empty_cache()
+    c5 = None
+    if not args.no_c5:
+        c5 = run_c5_leg(args, rank, world, dev, barrier, max_over_ranks, gather)
 
     cpu = measure_cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if world > 1:
         dist.barrier()
+    if dist.is_initialized():
         dist.destroy_process_group()
     if rank != 0:
         return 0
@@ -279,12 +569,13 @@ def run_ours(args, rank, world, local_rank):
     fl_step_total = 12.0 * H * B * D * E
     value = fl_step_total * n / (total_ms / 1e3) / 1e12
     peaks, peak_src = load_peaks()
-    peak_sus = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
-    peak_burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    peak, peak_why = select_peak(clocks, peaks, peak_src)
     bwd_fl = 8.0 * Hl * B * D * E
     fwd_fl = 4.0 * Hl * B * D * E
     bwd_tf = bwd_fl / (bwd_avg / 1e3) / 1e12
     fwd_tf = fwd_fl / (fwd_avg / 1e3) / 1e12
+    step_tf_gpu = value / world
+    exec_fl = (14.0 if bwd_mode == 1 else 18.0) * H * B * D * E
     # DRAM bytes of the backward's launches (ncu, per head, scaled to this launch's heads)
     traffic = None
     tp = ROOT / "profiles" / "roofline_traffic.json"
@@ -312,27 +603,44 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": WORKLOAD_NAME, "H": H, "B": B, "D": D, "E": E, "activation": act,
                    "heads_per_gpu": Hl, "parallelism": f"head-sharded x{world} (no communication)",
                    "l2": "inputs larger than L2 every step (X and dO are 2x64-512 MiB per GPU); no flush"},
+        "parity": parity,
         "roofline": {
             "bound": "tensor", "kernel": "fmlp_bwd: " + bwd_kernels,
-            "achieved": round(bwd_tf, 2), "peak": peak_sus, "unit": "TFLOP/s",
-            "frac": round(bwd_tf / peak_sus, 4), "traffic": traffic,
-            "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step loop)",
+            "achieved": round(bwd_tf, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+            "frac": round(bwd_tf / peak, 4), "traffic": traffic,
+            "peak_source": peak_why,
             "algorithmic_flops_per_launch": bwd_fl,
+            "frac_fwd": round(fwd_tf / peak, 4), "frac_step_per_gpu": round(step_tf_gpu / peak, 4),
+            "frac_executed_step_per_gpu": round(exec_fl * n / world / (total_ms / 1e3) / 1e12 / peak, 4),
             "bwd_mode": "dz-store" if bwd_mode == 1 else "recompute", "bwd_dw_splits": bwd_splits,
         },
         "fwd_ms": round(fwd_avg, 4), "bwd_ms": round(bwd_avg, 4),
         "fwd_tflops": round(fwd_tf, 2), "bwd_tflops": round(bwd_tf, 2),
-        "frac_of_measured_burst": round(value / world / peak_burst, 4),
-        "frac_of_spec_2250": round(value / world / SPEC_BF16_TFLOPS, 4),
+        "frac_of_spec_2250": round(step_tf_gpu / SPEC_BF16_TFLOPS, 4),
         # tensor FLOPs the kernels execute: forward 4, backward 8 for the dW programs (Z^T,
         # dH^T, dW1, dW2) plus 2 (dX GEMM) in the dZ-store mode or 6 (dX programs) otherwise
-        "executed_tensor_flops_per_step": (14.0 if bwd_mode == 1 else 18.0) * H * B * D * E,
+        "executed_tensor_flops_per_step": exec_fl,
+        "bwd_recompute": {"ms": round(rec_ms, 4), "tflops": round(bwd_fl / (rec_ms / 1e3) / 1e12, 2),
+                          "dw_splits": rsplits, "launches": rlaunch,
+                          "what": "the unified backward with the reference's dW/dX program-ID split "
+                                  "(low_memory_backward: dX programs recompute Z and dH), timed alone"},
+        "peak_mem_bytes": {"dz_store": int(peaks_mem[0]), "recompute": int(peaks_mem[1]),
+                           "inputs": int(inputs_bytes),
+                           "how": "torch.cuda.max_memory_allocated above the resident inputs over one fwd+bwd "
+                                  "(outputs and workspace included), max over ranks, as example.py measures it"},
         "cpu_baseline": cpu,
         "e2e": {"value": round(fl_step_total * n_e2e / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n_e2e,
                 "path": "flashmlp_b200.host.HostPipeline.run: pinned host X, W1, W2, dO in; O, dX, dW1, dW2 "
                         f"back to pinned host memory; groups of {hpg} head(s) pipelined (copy-in / flashmlp_fwd "
-                        "+ flashmlp_bwd / copy-out on three streams)"},
+                        "+ flashmlp_bwd / copy-out on three streams)",
+                "copy_only_gbs": {"h2d": [round(r[0], 1) for r in rates], "d2h": [round(r[1], 1) for r in rates],
+                                  "what": "per rank, all ranks at once: the step's bytes between the same pinned "
+                                          "buffers and the device, H2D and D2H concurrently on two streams, no kernels"},
+                "copy_bound_ms": round(max(h2d / (min(r[0] for r in rates) * 1e9),
+                                           d2h / (min(r[1] for r in rates) * 1e9)) * 1e3, 3),
+                "numa": numa},
+        "c5": c5,
         "gpu_launches": launches_per_step * n,
         "clocks": clocks,
         "device_status": status,
@@ -341,86 +649,110 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
-C5 = dict(H=8, B=131072, D=256, E=1024, activation="sigmoid", dtype="f16")
-C5_NAME = "C5 batch-sharded training step H=8 B=131072 D=256 E=1024 fp16 sigmoid"
-
-
-def run_c5(args, rank, world, local_rank):
-    """data-parallel training step (fwd + bwd on B/N rows per GPU, dW
-    all-reduce over NVLink, SGD). --allreduce fused: FusedBatchShardedTrainer (fp32 partials,
-    fmlp_grad_allreduce_sgd); nccl: batch_sharded_train_step (NCCL all-reduce + update)."""
+def run_c5_leg(args, rank, world, dev, barrier, max_over_ranks, gather):
+    """BASELINE config 5 at this N: each rank owns B/N rows, runs fwd + bwd, and the dW are
+    summed over ranks before an SGD step. Two variants: the fused NVLink all-reduce + SGD
+    (FusedBatchShardedTrainer, fp32 partials) and NCCL all-reduce + fmlp_sgd_update
+    (batch_sharded_train_step). Before timing, one step of each is checked."""
     import torch
     import torch.distributed as dist
 
     import flashmlp_b200 as F
     from flashmlp_b200 import sharding
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ.setdefault("MASTER_PORT", "29517")
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
-                            timeout=datetime.timedelta(seconds=120))
+    if not dist.is_initialized():  # N = 1: a one-rank group (the trainer's plumbing needs one)
+        dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1, device_id=dev)
     H, B, D, E = (C5[k] for k in "HBDE")
     act, dt, lr = C5["activation"], torch.float16, 1e-4
     b0, b1 = sharding.shard_range(B, world, rank)
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
     x = torch.randn(H, b1 - b0, D, device=dev, generator=g).to(dt)
     do = torch.randn(H, b1 - b0, D, device=dev, generator=g).to(dt)
     gw = torch.Generator(device=dev).manual_seed(7)  # replicas start equal
-    w1 = (torch.randn(H, D, E, device=dev, generator=gw) / D ** 0.5).to(dt)
-    w2 = (torch.randn(H, E, D, device=dev, generator=gw) / E ** 0.5).to(dt)
-    fused = args.allreduce == "fused"
-    tr = sharding.FusedBatchShardedTrainer(w1, w2) if fused else None
-
-    def step():
-        if fused:
-            tr.step(x, do, act, lr)
-        else:
-            sharding.batch_sharded_train_step(x, do, w1, w2, act, lr)
-
-    for _ in range(args.warmup):
-        step()
-    dist.barrier()
-    torch.cuda.synchronize()
-    n = args.steps
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(range(world)) if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(n):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    clocks = sampler.stop() if sampler else None
-    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
-    status = F._lib.lib().fmlp_device_status(1)
-    if tr is not None:
-        tr.close()
-    dist.barrier()
-    dist.destroy_process_group()
-    if rank != 0:
-        return 0
+    w1_0 = (torch.randn(H, D, E, device=dev, generator=gw) / D ** 0.5).to(dt)
+    w2_0 = (torch.randn(H, E, D, device=dev, generator=gw) / E ** 0.5).to(dt)
     fl = 12.0 * H * B * D * E
-    line = {
-        "metric": METRIC, "value": round(fl * n / (total_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
-        "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": round(total_ms / n, 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": C5_NAME, "H": H, "B": B, "D": D, "E": E, "activation": act,
-                   "rows_per_gpu": b1 - b0, "parallelism": f"batch-sharded x{world}",
-                   "allreduce": "fused fmlp_grad_allreduce_sgd (NVLink peer memory)" if fused
-                   else "NCCL all-reduce + fmlp_sgd_update",
-                   "l2": "inputs larger than L2 every step; no flush"},
-        "clocks": clocks, "device_status": status,
-    }
-    print(json.dumps(line), flush=True)
-    return 0
+    out = {"config": C5_NAME, "rows_per_gpu": b1 - b0}
+    n = args.steps
+
+    def replicas_equal(w1, w2):
+        ws = torch.cat([w1.reshape(-1), w2.reshape(-1)])
+        if world == 1:
+            return True
+        parts = [torch.empty_like(ws) for _ in range(world)]
+        dist.all_gather(parts, ws)
+        return all(torch.equal(parts[0], p) for p in parts[1:])
+
+    for variant in ("fused", "nccl"):
+        w1, w2 = w1_0.clone(), w2_0.clone()
+        tr = sharding.FusedBatchShardedTrainer(w1, w2) if variant == "fused" else None
+        # ---- check one step: the update equals the fixed-order fp32 sum of every rank's
+        # partial gradient (fused: bit for bit; NCCL: within fp32 summation-order error)
+        if variant == "fused":
+            _, part = F.flashmlp_bwd_dw_f32(x, tr.w1, tr.w2, do, act)
+        else:
+            _, pd1, pd2 = F.flashmlp_bwd(x, w1, w2, do, act)
+            part = torch.cat([pd1.reshape(-1).float(), pd2.reshape(-1).float()])
+        if world > 1:
+            parts = [torch.empty_like(part) for _ in range(world)]
+            dist.all_gather(parts, part)
+        else:
+            parts = [part]
+        gsum = parts[0].clone()
+        for p_ in parts[1:]:
+            gsum += p_
+        n1 = w1.numel()
+        rw1 = (w1_0.float() - lr * gsum[:n1].view(w1.shape)).to(dt)
+        rw2 = (w2_0.float() - lr * gsum[n1:].view(w2.shape)).to(dt)
+        if variant == "fused":
+            tr.step(x, do, act, lr)  # raises if the all-reduce failed on any rank
+            upd_ok = torch.equal(tr.w1, rw1) and torch.equal(tr.w2, rw2)
+            same = replicas_equal(tr.w1, tr.w2)
+        else:
+            _, _, g1, g2 = sharding.batch_sharded_train_step(x, do, w1, w2, act, lr)
+            gflat = torch.cat([g1.reshape(-1), g2.reshape(-1)])
+            tol = 1e-5 * gsum.abs().max().item() * world
+            upd_ok = bool(((gflat - gsum).abs() <= tol).all())
+            same = replicas_equal(w1, w2)
+        del parts, gsum, part, rw1, rw2
+        checks = gather([1.0 if upd_ok else 0.0, 1.0 if same else 0.0])
+
+        def step():
+            if tr is not None:
+                tr.step(x, do, act, lr, check=False)
+            else:
+                sharding.batch_sharded_train_step(x, do, w1, w2, act, lr)
+
+        for _ in range(args.warmup):
+            step()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            step()
+        e1.record()
+        barrier()
+        (ms,) = max_over_ranks([e0.elapsed_time(e1) / n])
+        ok_after = True
+        if tr is not None:
+            ok_after = tr.status() == 0
+            same_after = replicas_equal(tr.w1, tr.w2)
+            tr.close()
+        else:
+            same_after = replicas_equal(w1, w2)
+        after = gather([1.0 if ok_after else 0.0, 1.0 if same_after else 0.0])
+        out[variant] = {
+            "ms_per_step": round(ms, 4), "tflops": round(fl / (ms / 1e3) / 1e12, 2),
+            "update_matches_sum_of_partials": all(c[0] == 1.0 for c in checks),
+            "replicas_bit_identical": all(c[1] == 1.0 for c in checks) and all(a[1] == 1.0 for a in after),
+            "allreduce_status_ok": all(a[0] == 1.0 for a in after),
+            "allreduce": ("fmlp_grad_allreduce_sgd: fixed-order fp32 sum over NVLink peer memory + SGD, "
+                          "replicas written by the owning rank") if variant == "fused"
+            else "NCCL all-reduce (fp32) + fmlp_sgd_update",
+        }
+        del w1, w2, tr
+        torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -430,9 +762,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["c4", "c5"], default="c4",
-                    help="c4 (default, the headline): head-sharded fwd+bwd; c5: batch-sharded training step")
-    ap.add_argument("--allreduce", choices=["fused", "nccl"], default="fused", help="c5 only")
+    ap.add_argument("--no-c5", action="store_true", help="skip the C5 batch-sharded leg")
+    ap.add_argument("--no-triton", action="store_true", help="reference arm: skip the Triton-on-GPU timing")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -442,9 +773,7 @@ def main():
     if world != args.gpus:
         print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
     if args.impl == "reference":
-        return run_reference(args, rank)
-    if args.workload == "c5":
-        return run_c5(args, rank, world, local_rank)
+        return run_reference(args, rank, world)
     return run_ours(args, rank, world, local_rank)
 
 

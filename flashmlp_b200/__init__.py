@@ -5,14 +5,15 @@ flashmlp_bwd, FlashMLPFunction, FlashMLP, plus the plain-PyTorch PyTorchMLP,
 flashmlp_torch_fwd and flashmlp_torch_bwd it also exports. Multi-GPU wrappers live in
 flashmlp_b200.sharding.
 """
-from .api import (FlashMLP, FlashMLPFunction, FlashMLPSharedInputFunction, activation_code, flashmlp_bwd,
-                  flashmlp_bwd_dw_f32, flashmlp_bwd_shared_x, flashmlp_fwd, flashmlp_fwd_shared_x,
-                  low_memory_backward)
+from .api import (FlashMLP, FlashMLPFunction, FlashMLPSharedInputFunction, activation_code,
+                  backward_workspace_limit, flashmlp_bwd, flashmlp_bwd_dw_f32, flashmlp_bwd_shared_x, flashmlp_fwd,
+                  flashmlp_fwd_shared_x, low_memory_backward)
 from .torch_reference import PyTorchMLP, flashmlp_torch_bwd, flashmlp_torch_fwd
 from ._lib import FlashMLPError
 
 __all__ = [
     "low_memory_backward",
+    "backward_workspace_limit",
     "flashmlp_fwd",
     "flashmlp_bwd",
     "FlashMLPFunction",

@@ -24,7 +24,10 @@ FMLP_ERR_UNSUPPORTED_D = 3
 FMLP_ERR_UNSUPPORTED_E = 4
 FMLP_ERR_DEVICE_TIMEOUT = 10
 FMLP_ERR_SCRATCH_LIMIT = 11
+FMLP_ERR_PEER_ABORT = 12
 FMLP_MAX_PEERS = 8
+FMLP_PEER_FLAG_WORDS = 32   # uint32 words of each rank's flag array
+FMLP_PEER_STATUS_WORD = 16  # this rank's call status in its own flag array
 FMLP_IPC_HANDLE_BYTES = 64
 
 # Every symbol the header declares, with (restype, argtypes).

@@ -62,7 +62,24 @@ def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
     return ctypes.c_void_p(t.data_ptr())
 
 
-_LOW_MEMORY = threading.local()
+_WS_LIMIT = threading.local()
+
+
+@contextlib.contextmanager
+def backward_workspace_limit(nbytes):
+    """Within this context (per thread) the backward entry points ask the library for at
+    most `nbytes` of workspace, never less than fmlp_bwd_workspace_size_min. The library
+    then runs the dZ-store mode in head groups whose dZ^T tiles fit in it (one group
+    reuses the workspace after the other), or the recompute mode if fewer than
+    min(H, 4) heads' tiles fit. `None` lifts the limit: the fastest mode, whose transient
+    is 2*H*E*B bytes (8 GiB for 32 heads with B = 65536 and E = 2048) plus split partials,
+    in groups of at most 8 GiB."""
+    prev = getattr(_WS_LIMIT, "v", None)
+    _WS_LIMIT.v = None if nbytes is None else max(0, int(nbytes))
+    try:
+        yield
+    finally:
+        _WS_LIMIT.v = prev
 
 
 @contextlib.contextmanager
@@ -70,20 +87,18 @@ def low_memory_backward(enabled: bool = True):
     """Within this context (per thread) the backward entry points ask the library for its
     least workspace (fmlp_bwd_workspace_size_min), which selects the recompute mode: the dX
     programs recompute Z and dH rather than read the dZ^T tiles that the dW programs store
-    in the dZ-store mode. It saves that transient (2*H*E*B bytes, 8 GiB for 32 heads with
-    B = 65536 and E = 2048) at the cost of the recomputed products."""
-    prev = getattr(_LOW_MEMORY, "on", False)
-    _LOW_MEMORY.on = bool(enabled)
-    try:
+    in the dZ-store mode. It saves that transient at the cost of the recomputed products.
+    Equivalent to backward_workspace_limit(0)."""
+    with backward_workspace_limit(0 if enabled else getattr(_WS_LIMIT, "v", None)):
         yield
-    finally:
-        _LOW_MEMORY.on = prev
 
 
 def _bwd_workspace_bytes(L, H: int, B: int, D: int, E: int, dt: int) -> int:
-    if getattr(_LOW_MEMORY, "on", False):
-        return int(L.fmlp_bwd_workspace_size_min(H, B, D, E, dt))
-    return int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
+    full = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
+    lim = getattr(_WS_LIMIT, "v", None)
+    if lim is None or lim >= full:
+        return full
+    return max(int(L.fmlp_bwd_workspace_size_min(H, B, D, E, dt)), lim)
 
 
 def flashmlp_fwd(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,

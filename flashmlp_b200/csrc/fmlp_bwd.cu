@@ -850,6 +850,25 @@ size_t bwd_dz_workspace_bytes(int H, int B, int D, int E, int sm_count, int elem
   return dz + (s > 1 ? size_t(2) * s * size_t(H) * D * E * sizeof(float) : 0);
 }
 
+int bwd_dz_group_heads(int H, int B, int D, int E, int sm_count, int elem_bytes, size_t workspace_bytes) {
+  if (H <= 0) return 0;
+  const size_t one = bwd_dz_bytes(1, B, D, E, sm_count, elem_bytes);
+  if (one == 0) return 0;  // the mode does not apply, or one head alone exceeds the cap
+  long long g = H;
+  if ((long long)(kDzCapBytes / one) < g) g = (long long)(kDzCapBytes / one);
+  if ((long long)(workspace_bytes / one) < g) g = (long long)(workspace_bytes / one);
+  const long long floor_g = H < kDzMinGroupHeads ? H : kDzMinGroupHeads;
+  for (; g >= floor_g && g >= 1; --g) {
+    if (bwd_dz_workspace_bytes(int(g), B, D, E, sm_count, elem_bytes) > workspace_bytes) continue;
+    // as many groups as this size needs, with the heads spread evenly over them
+    const long long n = (H + g - 1) / g, even = (H + n - 1) / n;
+    if (even < g && bwd_dz_workspace_bytes(int(even), B, D, E, sm_count, elem_bytes) <= workspace_bytes)
+      return int(even);
+    return int(g);
+  }
+  return 0;
+}
+
 int bwd_smem_bytes(int dp) {
   switch (dp) {
     case 64: return BwdCfg<64>::SMEM;

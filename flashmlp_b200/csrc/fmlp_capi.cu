@@ -20,6 +20,7 @@ constexpr int kMaxDevices = 64;
 
 struct DeviceInfo {
   bool init = false;
+  void* ctx = nullptr;  // the context the cached device addresses belong to
   int sm_count = 0;
   int cc_major = 0;
   uint32_t* status = nullptr;
@@ -29,12 +30,40 @@ std::mutex g_mu;
 DeviceInfo g_dev[kMaxDevices];
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
+}  // namespace
+
+// The calling thread's current CUDA context (cuCtxGetCurrent through the runtime's
+// driver entry point), or nullptr if there is none or the lookup fails. Device addresses
+// of __device__ symbols belong to a context: after cudaDeviceReset the primary context
+// is a new one, and addresses cached for the old one would dangle.
+void* current_context() {
+  static PFN_cuCtxGetCurrent_v4000 fn = []() -> PFN_cuCtxGetCurrent_v4000 {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+  }();
+  CUcontext c = nullptr;
+  if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
+namespace {
+
 int device_info(DeviceInfo** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FMLP_ERR_CUDA;
+  void* ctx = current_context();
+  if (ctx == nullptr) {  // no context yet on this thread: make the device's primary one current
+    cudaFree(nullptr);
+    ctx = current_context();
+  }
   std::lock_guard<std::mutex> lk(g_mu);
   DeviceInfo& d = g_dev[dev];
-  if (!d.init) {
+  if (!d.init || d.ctx != ctx) {
+    d.init = false;
     if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return FMLP_ERR_CUDA;
     if (cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
@@ -51,6 +80,7 @@ int device_info(DeviceInfo** out) {
         return FMLP_ERR_TMA;
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
+    d.ctx = ctx;
     d.init = true;
   }
   if (d.cc_major != 10) return FMLP_ERR_DEVICE;
@@ -95,29 +125,38 @@ size_t elem_bytes(int dtype) { return dtype == FMLP_DTYPE_F32 ? 4 : 2; }
 int cuda_rc(cudaError_t e) { return e == cudaSuccess ? FMLP_OK : FMLP_ERR_CUDA; }
 
 // What a backward call runs for a given workspace: the dZ-store mode when the workspace
-// holds the dZ^T tiles (and their split-dW partials) and the mode applies, otherwise the
-// recompute mode, which needs `need` bytes (0 unless its dW programs split). One rule for
-// fmlp_bwd and fmlp_bwd_plan. `usable`: the workspace pointer is non-null and 16-byte
-// aligned (fmlp_bwd_plan assumes it is).
+// holds the dZ^T tiles (and their split-dW partials) of a group of at least
+// min(H, kDzMinGroupHeads) heads and the mode applies, otherwise the recompute mode,
+// which needs `need` bytes (0 unless its dW programs split). In the dZ-store mode the
+// heads run in groups of `group` that reuse the workspace (one group when it holds all
+// heads). One rule for fmlp_bwd and fmlp_bwd_plan. `usable`: the workspace pointer is
+// non-null and 16-byte aligned (fmlp_bwd_plan assumes it is). `grouping`: the call may run
+// in head groups (not the shared-input form, whose dX sums over heads, nor the fp32-dW
+// form, whose dW2 block follows all heads' dW1).
 struct BwdPlan {
   bool dz = false;
   int splits = 1;
+  int group = 0;        // heads per launch: H, or the group size in the dZ-store mode
   size_t dz_bytes = 0;  // dZ^T region at the start of the workspace (dZ-store mode)
 };
 
-int plan_bwd(int H, int B, int D, int E, bool f32, bool allow_dz, int sm_count, size_t workspace_bytes,
-             bool usable, BwdPlan* p) {
+int plan_bwd(int H, int B, int D, int E, bool f32, bool allow_dz, bool grouping, int sm_count,
+             size_t workspace_bytes, bool usable, BwdPlan* p) {
   const size_t need = f32 ? bwd_workspace_bytes_tf32(H, B, D, E, sm_count) : bwd_workspace_bytes(H, B, D, E, sm_count);
   const int esz = f32 ? 4 : 2;  // dZ is stored in the input dtype (fp32 stays fp32)
-  const size_t ws_dz = allow_dz ? bwd_dz_workspace_bytes(H, B, D, E, sm_count, esz) : 0;
-  p->dz = ws_dz != 0 && workspace_bytes >= ws_dz && usable;
-  if (!p->dz && (workspace_bytes < need || (need && !usable))) return FMLP_ERR_WORKSPACE;
-  if (p->dz) {
-    p->splits = f32 ? bwd_dz_splits_tf32(H, B, D, E, sm_count) : bwd_dz_splits(H, B, D, E, sm_count);
-    p->dz_bytes = bwd_dz_bytes(H, B, D, E, sm_count, esz);
-  } else {
-    p->splits = need ? (f32 ? bwd_dw_splits_tf32(H, B, D, E, sm_count) : bwd_dw_splits(H, B, D, E, sm_count)) : 1;
+  p->group = H;
+  if (allow_dz && usable) {
+    const int g = bwd_dz_group_heads(H, B, D, E, sm_count, esz, workspace_bytes);
+    if (g > 0 && (grouping || g == H)) {
+      p->dz = true;
+      p->group = g;
+      p->splits = f32 ? bwd_dz_splits_tf32(g, B, D, E, sm_count) : bwd_dz_splits(g, B, D, E, sm_count);
+      p->dz_bytes = bwd_dz_bytes(g, B, D, E, sm_count, esz);
+      return FMLP_OK;
+    }
   }
+  if (workspace_bytes < need || (need && !usable)) return FMLP_ERR_WORKSPACE;
+  p->splits = need ? (f32 ? bwd_dw_splits_tf32(H, B, D, E, sm_count) : bwd_dw_splits(H, B, D, E, sm_count)) : 1;
   return FMLP_OK;
 }
 
@@ -172,6 +211,9 @@ const char* fmlp_error_string(int code) {
     case FMLP_ERR_SCRATCH_LIMIT:
       return "shape needs more scratch than fmlp_bwd_noalloc's static device buffer "
              "(FMLP_NOALLOC_SCRATCH_BYTES); call fmlp_bwd with a workspace";
+    case FMLP_ERR_PEER_ABORT:
+      return "a rank of the fused all-reduce group gave up on a barrier (now or in an earlier call); "
+             "every rank should stop";
   }
   return "unknown error";
 }
@@ -249,8 +291,11 @@ size_t fmlp_bwd_workspace_size(int H, int B, int D, int E, int dtype) {
   if (D > 256 || check_common(H, B, D, E, dtype) || D % 16 != 0 || E % 8 != 0) return least;
   DeviceInfo* dev = nullptr;
   if (device_info(&dev)) return 0;
-  const size_t dz = bwd_dz_workspace_bytes(H, B, D, E, dev->sm_count, dtype == FMLP_DTYPE_F32 ? 4 : 2);
-  return dz ? dz : least;
+  const int esz = dtype == FMLP_DTYPE_F32 ? 4 : 2;
+  // the largest head group the cap allows (all heads when they fit one launch)
+  const int g = bwd_dz_group_heads(H, B, D, E, dev->sm_count, esz, ~size_t(0));
+  const size_t dz = g > 0 ? bwd_dz_workspace_bytes(g, B, D, E, dev->sm_count, esz) : 0;
+  return dz > least ? dz : least;
 }
 
 int fmlp_bwd_plan(int H, int B, int D, int E, int dtype, size_t workspace_bytes, int* mode, int* splits,
@@ -263,11 +308,12 @@ int fmlp_bwd_plan(int H, int B, int D, int E, int dtype, size_t workspace_bytes,
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
   BwdPlan p;  // the choice fmlp_bwd makes for a non-null, 16-byte aligned workspace
-  if ((rc = plan_bwd(H, B, D, E, f32, true, dev->sm_count, workspace_bytes, true, &p))) return rc;
+  if ((rc = plan_bwd(H, B, D, E, f32, true, true, dev->sm_count, workspace_bytes, true, &p))) return rc;
   const bool empty = H == 0 || B == 0 || D == 0 || E == 0;
+  const int groups = p.dz ? (H + p.group - 1) / p.group : 1;
   if (mode) *mode = p.dz ? 1 : 0;
   if (splits) *splits = p.splits;
-  if (launches) *launches = empty ? 0 : 1 + (p.dz ? 1 : 0) + (p.splits > 1 ? 1 : 0);
+  if (launches) *launches = empty ? 0 : groups * (1 + (p.dz ? 1 : 0) + (p.splits > 1 ? 1 : 0));
   return FMLP_OK;
 }
 
@@ -275,38 +321,12 @@ int fmlp_bwd_plan(int H, int B, int D, int E, int dtype, size_t workspace_bytes,
 
 namespace {
 
-// Shared body of fmlp_bwd (dW rounded into dw1/dw2) and fmlp_bwd_dw_f32 (dW as unrounded
-// fp32 into dwf = dW1 (H,D,E) followed by dW2 (H,E,D)).
-int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1, void* dw2,
-             float* dwf, void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype, int act,
-             int shared_x, void* stream, bool allow_dz = true) {
-  int rc = check_common(H, B, D, E, dtype);
-  if (rc) return rc;
+// One backward launch sequence over Hg heads whose tensors start at the given pointers.
+int bwd_launch_group(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1, void* dw2,
+                     float* dwf, void* workspace, const BwdPlan& plan, int H, int B, int D, int E, int dtype, int act,
+                     int shared_x, const DeviceInfo* dev, cudaStream_t st) {
+  int rc = FMLP_OK;
   const bool f32 = dtype == FMLP_DTYPE_F32;
-  if (f32 && shared_x) return FMLP_ERR_UNSUPPORTED_DTYPE;
-  if (D % 16 != 0 || D > (shared_x || f32 ? 128 : 256)) return FMLP_ERR_UNSUPPORTED_D;
-  if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
-  if (shared_x && H == 0) return FMLP_ERR_INVALID_SHAPE;
-  DeviceInfo* dev = nullptr;
-  if ((rc = device_info(&dev))) return rc;
-  // dZ-store mode when the workspace holds dZ^T (the size fmlp_bwd_workspace_size asks
-  // for); otherwise the dX programs recompute Z and dH
-  BwdPlan plan;
-  if ((rc = plan_bwd(H, B, D, E, f32, allow_dz, dev->sm_count, workspace_bytes,
-                     workspace != nullptr && aligned16(workspace), &plan)))
-    return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (H == 0 || D == 0) return FMLP_OK;
-  const size_t esz = elem_bytes(dtype);
-  if (E == 0) return cuda_rc(cudaMemsetAsync(dx, 0, size_t(shared_x ? 1 : H) * B * D * esz, st));
-  if (B == 0) {
-    if (dwf) return cuda_rc(cudaMemsetAsync(dwf, 0, size_t(2) * H * D * E * sizeof(float), st));
-    if ((rc = cuda_rc(cudaMemsetAsync(dw1, 0, size_t(H) * D * E * esz, st)))) return rc;
-    return cuda_rc(cudaMemsetAsync(dw2, 0, size_t(H) * E * D * esz, st));
-  }
-  if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(dO) || !aligned16(dx))
-    return FMLP_ERR_MISALIGNED;
-  if (dwf ? !aligned16(dwf) : (!aligned16(dw1) || !aligned16(dw2))) return FMLP_ERR_MISALIGNED;
   BwdLaunch a{};
   a.dp = round_dp(D);
   const int bf = dtype == FMLP_DTYPE_BF16;
@@ -350,6 +370,53 @@ int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void
   a.status = dev->status;
   a.stream = st;
   return cuda_rc(f32 ? launch_bwd_tf32(a) : launch_bwd(a));
+}
+
+// Shared body of fmlp_bwd (dW rounded into dw1/dw2) and fmlp_bwd_dw_f32 (dW as unrounded
+// fp32 into dwf = dW1 (H,D,E) followed by dW2 (H,E,D)).
+int bwd_impl(const void* x, const void* w1, const void* w2, const void* dO, void* dx, void* dw1, void* dw2,
+             float* dwf, void* workspace, size_t workspace_bytes, int H, int B, int D, int E, int dtype, int act,
+             int shared_x, void* stream, bool allow_dz = true) {
+  int rc = check_common(H, B, D, E, dtype);
+  if (rc) return rc;
+  const bool f32 = dtype == FMLP_DTYPE_F32;
+  if (f32 && shared_x) return FMLP_ERR_UNSUPPORTED_DTYPE;
+  if (D % 16 != 0 || D > (shared_x || f32 ? 128 : 256)) return FMLP_ERR_UNSUPPORTED_D;
+  if (E % 8 != 0) return FMLP_ERR_UNSUPPORTED_E;
+  if (shared_x && H == 0) return FMLP_ERR_INVALID_SHAPE;
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+  // dZ-store mode when the workspace holds dZ^T (the size fmlp_bwd_workspace_size asks
+  // for); otherwise the dX programs recompute Z and dH
+  BwdPlan plan;
+  if ((rc = plan_bwd(H, B, D, E, f32, allow_dz, !shared_x && dwf == nullptr, dev->sm_count, workspace_bytes,
+                     workspace != nullptr && aligned16(workspace), &plan)))
+    return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (H == 0 || D == 0) return FMLP_OK;
+  const size_t esz = elem_bytes(dtype);
+  if (E == 0) return cuda_rc(cudaMemsetAsync(dx, 0, size_t(shared_x ? 1 : H) * B * D * esz, st));
+  if (B == 0) {
+    if (dwf) return cuda_rc(cudaMemsetAsync(dwf, 0, size_t(2) * H * D * E * sizeof(float), st));
+    if ((rc = cuda_rc(cudaMemsetAsync(dw1, 0, size_t(H) * D * E * esz, st)))) return rc;
+    return cuda_rc(cudaMemsetAsync(dw2, 0, size_t(H) * E * D * esz, st));
+  }
+  if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(dO) || !aligned16(dx))
+    return FMLP_ERR_MISALIGNED;
+  if (dwf ? !aligned16(dwf) : (!aligned16(dw1) || !aligned16(dw2))) return FMLP_ERR_MISALIGNED;
+  // one launch sequence per head group (one group unless the dZ-store mode runs in groups)
+  const int G = plan.group > 0 ? plan.group : H;
+  for (int g0 = 0; g0 < H; g0 += G) {
+    const int Hg = H - g0 < G ? H - g0 : G;
+    const size_t xo = shared_x ? 0 : size_t(g0) * B * D * esz, wo = size_t(g0) * D * E * esz;
+    rc = bwd_launch_group(static_cast<const char*>(x) + xo, static_cast<const char*>(w1) + wo,
+                          static_cast<const char*>(w2) + wo, static_cast<const char*>(dO) + xo,
+                          static_cast<char*>(dx) + xo, dw1 ? static_cast<char*>(dw1) + wo : nullptr,
+                          dw2 ? static_cast<char*>(dw2) + wo : nullptr, dwf, workspace, plan, Hg, B, D, E, dtype,
+                          act, shared_x, dev, st);
+    if (rc) return rc;
+  }
+  return FMLP_OK;
 }
 
 }  // namespace

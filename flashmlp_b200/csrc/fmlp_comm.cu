@@ -18,9 +18,20 @@
 //
 // The barriers are epoch counters: rank r writes the call's epoch into slot r of every
 // rank's flag array (st.release.sys) and waits until each slot of its own array has
-// reached it (ld.acquire.sys). Every wait is bounded (FMLP_WAIT_LIMIT_NS); on expiry the
-// kernel records a timeout in the device status word and returns, so a rank that never
-// arrives cannot hang the GPU. Only plain peer loads and stores are used (no multicast).
+// reached it (ld.acquire.sys). Every wait is bounded (FMLP_WAIT_LIMIT_NS).
+//
+// Failure: a rank whose wait runs out (a peer never arrived) or that sees a peer's abort
+// mark gives up. It writes a nonzero abort mark into its own abort slot of every rank's
+// flag array, records the reason in its own call-status word, skips its reduce slice and
+// publishes no further epoch. The abort marks are sticky: a peer that arrives late, or
+// calls again, finds the mark before it waits, fails at once with FMLP_ERR_PEER_ABORT and
+// touches no peer memory. So a call that returns a clean call status on a rank was
+// completed by every rank: each rank published epoch + 1 only after its own first barrier
+// passed and its slice was written. The call status belongs to the call (the first
+// barrier resets it); the device-wide status word of other kernels is not consulted, so
+// a timeout elsewhere in the process does not stop a later reduction. A group with an
+// abort mark set must be rebuilt (fresh, zeroed flag arrays); every rank should stop.
+// Only plain peer loads and stores are used (no multicast).
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -31,6 +42,9 @@
 
 namespace fmlp {
 namespace {
+
+static_assert(FMLP_PEER_STATUS_WORD >= 2 * FMLP_MAX_PEERS && FMLP_PEER_STATUS_WORD < FMLP_PEER_FLAG_WORDS,
+              "flag array: epoch slots, abort slots, then the call status");
 
 struct PeerSet {
   void* p[FMLP_MAX_PEERS];
@@ -46,25 +60,53 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// One warp: lane k publishes `epoch` in slot `rank` of rank k's flags, then waits for slot
-// k of this rank's flags to reach `epoch` (wrap-safe comparison).
-__global__ void fmlp_peer_barrier_kernel(PeerSet flags, int world, int rank, uint32_t epoch, uint32_t* status) {
+__device__ __forceinline__ uint32_t* flag_words(const PeerSet& f, int k) { return static_cast<uint32_t*>(f.p[k]); }
+
+// One warp, lane k < world speaks for rank k. `first`: the call's first barrier, which
+// starts the call status afresh; the second one keeps the first one's verdict.
+//   clean so far: publish `epoch` in slot `rank` of every rank's epoch slots, then wait
+//     until every epoch slot of this rank's array has reached `epoch` (wrap-safe), an
+//     abort mark appears, or the wait limit passes;
+//   failed (now or before): publish this rank's abort mark in every rank's array.
+__global__ void fmlp_peer_barrier_kernel(PeerSet flags, int world, int rank, uint32_t epoch, int first,
+                                         uint32_t* dev_status) {
   const int k = threadIdx.x;
-  if (k < world) {
-    __threadfence_system();  // this GPU's earlier writes to peers are visible first
-    st_release_sys(static_cast<uint32_t*>(flags.p[k]) + rank, epoch);
-  }
-  __syncwarp();
-  if (k >= world) return;
-  const uint32_t* mine = static_cast<const uint32_t*>(flags.p[rank]) + k;
-  const uint64_t t0 = global_timer_ns();
-  while (static_cast<int32_t>(ld_acquire_sys(mine) - epoch) < 0) {
-    if (global_timer_ns() - t0 > FMLP_WAIT_LIMIT_NS) {
-      atomicOr(status, kDevTimeout);
-      return;
+  uint32_t* own = flag_words(flags, rank);
+  volatile uint32_t* call_status = own + FMLP_PEER_STATUS_WORD;
+  uint32_t st = first ? 0u : *call_status;
+  const bool marked = k < world && ld_acquire_sys(own + FMLP_MAX_PEERS + k) != 0u;
+  if (__any_sync(0xffffffffu, marked) && st == 0u) st = FMLP_ERR_PEER_ABORT;
+  if (st == 0u) {
+    if (k < world) {
+      __threadfence_system();  // this GPU's earlier writes to peers are visible first
+      st_release_sys(flag_words(flags, k) + rank, epoch);
     }
-    __nanosleep(64);
+    __syncwarp();
+    bool done = k >= world, timed_out = false, aborted = false;
+    const uint64_t t0 = global_timer_ns();
+    while (!__all_sync(0xffffffffu, done)) {
+      if (!done) {
+        if (ld_acquire_sys(own + FMLP_MAX_PEERS + k) != 0u) {
+          aborted = done = true;
+        } else if (static_cast<int32_t>(ld_acquire_sys(own + k) - epoch) >= 0) {
+          done = true;
+        } else if (global_timer_ns() - t0 > FMLP_WAIT_LIMIT_NS) {
+          timed_out = done = true;
+        } else {
+          __nanosleep(64);
+        }
+      }
+    }
+    if (__any_sync(0xffffffffu, timed_out))
+      st = FMLP_ERR_DEVICE_TIMEOUT;
+    else if (__any_sync(0xffffffffu, aborted))
+      st = FMLP_ERR_PEER_ABORT;
   }
+  if (st != 0u) {
+    if (k < world) st_release_sys(flag_words(flags, k) + FMLP_MAX_PEERS + rank, 1u);
+    if (k == 0 && st == FMLP_ERR_DEVICE_TIMEOUT) atomicOr(dev_status, kDevTimeout);
+  }
+  if (k == 0) *call_status = st;
 }
 
 // Slice [lo4, hi4) of 4-element groups: fixed-order fp32 sum of every rank's gradient,
@@ -72,9 +114,9 @@ __global__ void fmlp_peer_barrier_kernel(PeerSet flags, int world, int rank, uin
 template <typename T>
 __global__ void __launch_bounds__(256)
     fmlp_allreduce_sgd_kernel(PeerSet w, PeerSet g, int world, int rank, long long lo4, long long hi4, float lr,
-                              const uint32_t* status) {
-  // A timed-out barrier means some rank did not arrive: touch no peer memory.
-  if (*reinterpret_cast<const volatile uint32_t*>(status) & kDevTimeout) return;
+                              const uint32_t* call_status) {
+  // The call's first barrier failed (a rank did not arrive or gave up): touch no peer memory.
+  if (*reinterpret_cast<const volatile uint32_t*>(call_status) != 0u) return;
   const uint2* wl = static_cast<const uint2*>(w.p[rank]);
   for (long long i = lo4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < hi4;
        i += (long long)gridDim.x * blockDim.x) {
@@ -161,25 +203,23 @@ int fmlp_grad_allreduce_sgd(void* const* peer_w, const float* const* peer_g, uin
   const long long n4 = n / 4, base = n4 / world, extra = n4 % world;
   const long long lo4 = rank * base + (rank < extra ? rank : extra);
   const long long hi4 = lo4 + base + (rank < extra ? 1 : 0);
-  if (world > 1) {
-    fmlp_peer_barrier_kernel<<<1, 32, 0, st>>>(f, world, rank, epoch, status);
-    if (cudaGetLastError() != cudaSuccess) return FMLP_ERR_CUDA;
-  }
+  const uint32_t* call_status = static_cast<const uint32_t*>(f.p[rank]) + FMLP_PEER_STATUS_WORD;
+  fmlp_peer_barrier_kernel<<<1, 32, 0, st>>>(f, world, rank, epoch, 1, status);
+  if (cudaGetLastError() != cudaSuccess) return FMLP_ERR_CUDA;
   if (hi4 > lo4) {
     long long blocks = (hi4 - lo4 + 255) / 256;
     const long long cap = (long long)sm_count * 4;
     if (blocks > cap) blocks = cap;
     if (dtype == FMLP_DTYPE_BF16)
       fmlp_allreduce_sgd_kernel<__nv_bfloat16><<<unsigned(blocks), 256, 0, st>>>(w, g, world, rank, lo4, hi4, lr,
-                                                                                  status);
+                                                                                  call_status);
     else
-      fmlp_allreduce_sgd_kernel<__half><<<unsigned(blocks), 256, 0, st>>>(w, g, world, rank, lo4, hi4, lr, status);
+      fmlp_allreduce_sgd_kernel<__half><<<unsigned(blocks), 256, 0, st>>>(w, g, world, rank, lo4, hi4, lr,
+                                                                         call_status);
     if (cudaGetLastError() != cudaSuccess) return FMLP_ERR_CUDA;
   }
-  if (world > 1) {
-    fmlp_peer_barrier_kernel<<<1, 32, 0, st>>>(f, world, rank, epoch + 1u, status);
-    if (cudaGetLastError() != cudaSuccess) return FMLP_ERR_CUDA;
-  }
+  fmlp_peer_barrier_kernel<<<1, 32, 0, st>>>(f, world, rank, epoch + 1u, 0, status);
+  if (cudaGetLastError() != cudaSuccess) return FMLP_ERR_CUDA;
   return FMLP_OK;
 }
 

@@ -74,6 +74,7 @@ cudaError_t launch_bwd_tf32(const BwdLaunch& a);
 int bwd256_smem_bytes();
 // SM count and device status word of the current device (fails if it is not an sm_100).
 int current_device_status(int* sm_count, uint32_t** status);
+void* current_context();  // the calling thread's current CUDA context (CUcontext), or nullptr
 
 // Split factor of the dW programs for a backward launch (1 = none) and the fp32 workspace
 // bytes it needs: 2 * splits * H * D * E * 4 when splits > 1.
@@ -86,14 +87,21 @@ int bwd_dz_splits_tf32(int H, int B, int D, int E, int sm_count);  // dZ-store m
 
 // dZ-store mode of the backward (16-bit inputs with D <= 256, fp32 inputs with D <= 128):
 // the dW programs also store dZ and a GEMM over E forms dX from it (fmlp_dxgemm.cu; fp32:
-// fmlp_tf32.cu). bwd_dz_bytes is the dZ workspace for elements of elem_bytes (0 when the
-// mode does not apply or would need more than kDzCapBytes); bwd_dz_splits the dW split
-// factor of that launch, whose fp32 partials follow the dZ region (bwd_dz_workspace_bytes
-// is the total).
+// fmlp_tf32.cu). bwd_dz_bytes is the dZ workspace of one launch over H heads for elements
+// of elem_bytes (0 when the mode does not apply or would need more than kDzCapBytes: the
+// kernels address a launch's dZ tiles with 32-bit element offsets); bwd_dz_splits the dW
+// split factor of that launch, whose fp32 partials follow the dZ region
+// (bwd_dz_workspace_bytes is the total). A backward call whose heads do not fit one such
+// launch, or whose caller gives a smaller workspace, runs the mode in head groups that
+// reuse the workspace: bwd_dz_group_heads is the group size for a workspace (0: the mode
+// does not apply, or fewer than min(H, kDzMinGroupHeads) heads fit, where the recompute
+// mode in one launch is the better choice).
 constexpr size_t kDzCapBytes = size_t(8) << 30;
+constexpr int kDzMinGroupHeads = 4;
 size_t bwd_dz_bytes(int H, int B, int D, int E, int sm_count, int elem_bytes = 2);
 int bwd_dz_splits(int H, int B, int D, int E, int sm_count);
 size_t bwd_dz_workspace_bytes(int H, int B, int D, int E, int sm_count, int elem_bytes = 2);
+int bwd_dz_group_heads(int H, int B, int D, int E, int sm_count, int elem_bytes, size_t workspace_bytes);
 
 // Body of fmlp_bwd; allow_dz = 0 keeps the recompute mode whatever the workspace size
 // (fmlp_bwd_noalloc).

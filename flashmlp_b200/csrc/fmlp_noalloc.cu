@@ -36,20 +36,25 @@ __device__ __align__(256) float g_fmlp_noalloc_scratch[kNoAllocScratchBytes / si
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void* g_scratch[kMaxDevices] = {};  // device address of the array, per device
+void* g_scratch[kMaxDevices] = {};      // device address of the array, per device
+void* g_scratch_ctx[kMaxDevices] = {};  // the context that address belongs to
 
 // Device address of this device's copy of the array. In host code the array's name only
 // stands in for the symbol; a kernel given it would read host memory or fault, so the
-// address comes from cudaGetSymbolAddress, once per device, with that device current.
+// address comes from cudaGetSymbolAddress, once per device and context, with that device
+// current. A new context on the device (after cudaDeviceReset) gets a new array, whose
+// address is looked up again.
 int scratch_for_current_device(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FMLP_ERR_CUDA;
+  void* ctx = current_context();
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_scratch[dev] == nullptr) {
+  if (g_scratch[dev] == nullptr || g_scratch_ctx[dev] != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_fmlp_noalloc_scratch) != cudaSuccess || p == nullptr)
       return FMLP_ERR_CUDA;
     g_scratch[dev] = p;
+    g_scratch_ctx[dev] = current_context();  // the symbol lookup made the context current
   }
   *out = g_scratch[dev];
   return FMLP_OK;

@@ -59,14 +59,14 @@ def main() -> None:
 
 
 def _allreduce(a, H, D, E, dt) -> None:
-    """One-rank fmlp_grad_allreduce_sgd (no barrier; the reduce + update over all n
+    """One-rank fmlp_grad_allreduce_sgd (barriers without peers; the reduce + update over all n
     weights) and fmlp_sgd_update, each `iters` times, on n = 2*H*D*E weights."""
     import ctypes
 
     n = 2 * H * D * E
     w = torch.randn(n, device="cuda").to(dt)
     g = torch.randn(n, device="cuda")
-    flags = torch.zeros(8, dtype=torch.int32, device="cuda")
+    flags = torch.zeros(_lib.FMLP_PEER_FLAG_WORDS, dtype=torch.int32, device="cuda")
     L = _lib.lib()
     arr = lambda t: (ctypes.c_void_p * 1)(ctypes.c_void_p(t.data_ptr()))
     code = _lib.FMLP_DTYPE_BF16 if dt == torch.bfloat16 else _lib.FMLP_DTYPE_F16

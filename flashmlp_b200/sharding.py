@@ -225,13 +225,15 @@ class FusedBatchShardedTrainer:
         with torch.cuda.device(dev):
             self._w = PeerBuffer(_align16(2 * self.n), group)
             self._g = PeerBuffer(_align16(4 * self.n), group)
-            self._f = PeerBuffer(_align16(4 * _lib.FMLP_MAX_PEERS), group)
+            self._f = PeerBuffer(_align16(4 * _lib.FMLP_PEER_FLAG_WORDS), group)
         wflat = self._w.view(0, (self.n,), w1.dtype, dev)
         self.w1 = wflat[: self.n1].view(self.shape1)
         self.w2 = wflat[self.n1:].view(self.shape2)
         self.w1.copy_(w1)
         self.w2.copy_(w2)
         self.grad = self._g.view(0, (self.n,), torch.float32, dev)  # this rank's fp32 dW1 || dW2
+        # this rank's flag array: epoch slots, abort marks, then the last call's status
+        self.flags = self._f.view(0, (_lib.FMLP_PEER_FLAG_WORDS,), torch.int32, dev)
         self.epoch = 0
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)  # every rank's buffers and zeroed flags exist before any use
@@ -251,12 +253,30 @@ class FusedBatchShardedTrainer:
                                            ctypes.c_void_p(stream))
         _lib.check(rc, "fmlp_grad_allreduce_sgd")
 
-    def step(self, x_local, do_local, activation: str = "", lr: float = 1e-3):
+    def status(self) -> int:
+        """Status of the last fused all-reduce call on this rank (waits for it to finish):
+        FMLP_OK, FMLP_ERR_DEVICE_TIMEOUT (a peer did not arrive in time) or
+        FMLP_ERR_PEER_ABORT (a rank gave up, in that call or an earlier one)."""
+        torch.cuda.current_stream(self.device).synchronize()
+        return int(self.flags[_lib.FMLP_PEER_STATUS_WORD].item())
+
+    def check(self) -> None:
+        """Raises FlashMLPError if the last fused all-reduce call failed on this rank. After
+        a failure the group's flag arrays carry an abort mark and every later call fails on
+        every rank: all ranks must stop (and rebuild the trainer to continue)."""
+        _lib.check(self.status(), "fmlp_grad_allreduce_sgd (device status of the call)")
+
+    def step(self, x_local, do_local, activation: str = "", lr: float = 1e-3, check: bool = True):
         """Forward + backward on this rank's rows, then the fused all-reduce + SGD.
-        Returns (o_local, dx_local)."""
+        Returns (o_local, dx_local). With check=True (the default) it waits for the step
+        and raises FlashMLPError if the all-reduce failed on any rank (a peer timed out or
+        gave up); with check=False the caller calls check() later, e.g. once after a
+        timed loop (a failure is sticky, so no failed step goes unnoticed)."""
         o = flashmlp_fwd(x_local, self.w1, self.w2, activation)
         dx, _ = flashmlp_bwd_dw_f32(x_local, self.w1, self.w2, do_local, activation, dw_out=self.grad)
         self.allreduce_sgd_(lr)
+        if check:
+            self.check()
         return o, dx
 
     def close(self):

@@ -49,6 +49,8 @@ extern "C" {
 #define FMLP_ERR_DEVICE_TIMEOUT 10  /* a kernel's bounded pipeline wait ran out        */
 #define FMLP_ERR_SCRATCH_LIMIT 11   /* fmlp_bwd_noalloc: shape needs more scratch than
                                        FMLP_NOALLOC_SCRATCH_BYTES                      */
+#define FMLP_ERR_PEER_ABORT 12      /* fmlp_grad_allreduce_sgd: a rank of the group gave
+                                       up on a barrier (now or in an earlier call)     */
 
 /*
  * Forward. Replaces flashmlp_fwd + flashmlp_fwd_kernel (flashmlp.py:428-477, :63-158).
@@ -159,16 +161,26 @@ int fmlp_sgd_update(void* w, const float* g, long long n, float lr, int dtype, v
  * memory; no reference counterpart (it replaces an NCCL all-reduce of dW1 || dW2 followed
  * by fmlp_sgd_update). One process per GPU, world <= FMLP_MAX_PEERS ranks on distinct GPUs
  * of one node. peer_w[k] (n 16-bit weights, rank k's replica), peer_g[k] (n fp32
- * gradients of rank k's rows) and peer_flags[k] (world uint32 counters, zero-initialised)
- * are rank k's buffers as mapped into this process (fmlp_ipc_open_handle; the own rank's
- * entries are its plain device pointers); the arrays themselves are host memory. Every
- * rank calls with the same n, lr, dtype and epoch, and a fresh epoch per call (two
- * counter values are used per call: epoch and epoch + 1). Rank r sums slice r of the
- * gradients over ranks 0..world-1 in that order in fp32, applies w = round(w - lr * g) and
- * stores the result into every replica; barriers before and after make every replica
- * complete when the call's work on `stream` ends. A peer that does not arrive within the
- * wait limit leaves FMLP_ERR_DEVICE_TIMEOUT in fmlp_device_status. n % 4 == 0.
+ * gradients of rank k's rows) and peer_flags[k] (FMLP_PEER_FLAG_WORDS uint32 words,
+ * zero-initialised when the group is formed) are rank k's buffers as mapped into this
+ * process (fmlp_ipc_open_handle; the own rank's entries are its plain device pointers);
+ * the arrays themselves are host memory. Every rank calls with the same n, lr, dtype and
+ * epoch, and a fresh epoch per call (two counter values are used per call: epoch and
+ * epoch + 1). Rank r sums slice r of the gradients over ranks 0..world-1 in that order in
+ * fp32, applies w = round(w - lr * g) and stores the result into every replica; barriers
+ * before and after make every replica complete when the call's work on `stream` ends.
+ * n % 4 == 0.
+ *
+ * Failure reporting: when the call's work on `stream` has ended, word
+ * FMLP_PEER_STATUS_WORD of this rank's own flag array holds the call's status: FMLP_OK
+ * (every rank completed the call), FMLP_ERR_DEVICE_TIMEOUT (a peer did not arrive within
+ * the wait limit; also recorded in fmlp_device_status) or FMLP_ERR_PEER_ABORT (a rank
+ * gave up, in this call or an earlier one). A rank that fails skips its slice and marks
+ * the failure in every rank's flag array (words FMLP_MAX_PEERS..2*FMLP_MAX_PEERS-1), so
+ * every later call of the group fails at once on every rank: all ranks should stop.
  */
+#define FMLP_PEER_FLAG_WORDS 32
+#define FMLP_PEER_STATUS_WORD 16
 #define FMLP_MAX_PEERS 8
 int fmlp_grad_allreduce_sgd(void* const* peer_w, const float* const* peer_g,
                             uint32_t* const* peer_flags, int world, int rank, long long n, float lr,

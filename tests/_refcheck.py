@@ -11,6 +11,22 @@ it covers fp32 accumulation order over K = B = 65536 rows and one-step flips of 
 16-bit rounded intermediates H and dZ. leaky_relu's derivative jumps at z = 0, so an
 element whose |z| is within the fp32 accumulation error may legitimately take the other
 branch; its possible contribution 0.99 |dh| |w| is added for those elements only.
+
+The elementwise bound is loose where K is large: at K = B = 65536 its kappa term is about
+a quarter of a typical |dW| element, so a uniform few-percent error, or one dropped
+128-row B tile, could pass it. Every check therefore also applies a norm-wise bound per
+head slice (dim 0 of a 3-D tensor, the whole tensor otherwise):
+
+    ||a - r||_F <= c * ||r||_F  (+ ||slack||_F for leaky_relu with fp32 inputs)
+
+with c = 5e-3 (bf16), 2e-3 (fp16), 3e-3 (fp32 inputs, TF32 products). The floor any
+16-bit result with fp32 accumulation has is its final rounding: about 1.5e-3 (bf16) and
+2e-4 (fp16) of ||r||_F for these value distributions (cuBLAS bf16 batched GEMMs on the
+same inputs measure that floor, tests/test_triton_reference_gpu.py). The constants are
+3x and 10x it. A uniform 2 % error, or one dropped 128-row B tile of a dW sum over
+65536 rows (about 4.4 %), fails it (tests/test_refcheck_cpu.py). Slices with fewer than
+NORM_MIN_ELEMS elements are checked elementwise only: a norm over a handful of elements
+says nothing more than the elements do.
 """
 from __future__ import annotations
 
@@ -19,6 +35,13 @@ import torch
 
 KAPPA = 2.0 ** -10
 Z_AMBIGUOUS = 1e-3
+NORM_C = {torch.bfloat16: 5e-3, torch.float16: 2e-3, torch.float32: 3e-3}
+NORM_MIN_ELEMS = 4096
+# largest norm-wise relative error seen per (dtype, kind) in this process; reported at the
+# end of a pytest session (tests/conftest.py)
+NORM_SEEN: dict = {}
+# free-form measurements the tests record for the same end-of-session report
+INFO: list = []
 
 
 def tol_for(dtype: torch.dtype, kind: str):
@@ -89,9 +112,54 @@ def ref_bwd(x, w1, w2, do, a):
         if dt == torch.float32:
             win = win + KAPPA * torch.bmm(xf.abs(), w1f.abs())
         amb = (z.abs() < win).float() * dh.abs() * 0.99
-        out["dx"][1] = out["dx"][1] + torch.bmm(amb, w1f.abs().transpose(1, 2)) / KAPPA
-        out["dw1"][1] = out["dw1"][1] + torch.bmm(xf.abs().transpose(1, 2), amb) / KAPPA
+        amb_dx = torch.bmm(amb, w1f.abs().transpose(1, 2))
+        amb_dw1 = torch.bmm(xf.abs().transpose(1, 2), amb)
+        out["dx"][1] = out["dx"][1] + amb_dx / KAPPA
+        out["dw1"][1] = out["dw1"][1] + amb_dw1 / KAPPA
+        if dt == torch.float32:
+            # TF32 products put about 2e-4 of the z values on the other side of 0, enough
+            # to move the norm of dX and dW1 by ~1e-2: the norm-wise check allows exactly
+            # those elements' possible contribution (16-bit inputs: fp32 accumulation
+            # error flips a negligible fraction, so no allowance)
+            out["dx"][1].fmlp_slack = amb_dx
+            out["dw1"][1].fmlp_slack = amb_dw1
     return {k: tuple(v) for k, v in out.items()}
+
+
+def norm_rel_errors(a: torch.Tensor, ref: torch.Tensor, slack=None):
+    """Per head slice (dim 0 of a 3-D tensor, else the whole tensor): (||a - r||_F -
+    ||slack||_F) / ||r||_F, for slices with at least NORM_MIN_ELEMS elements."""
+    a, ref = a.float(), ref.float()
+    if a.dim() != 3:
+        a, ref = a.reshape(1, -1), ref.reshape(1, -1)
+        slack = None if slack is None else slack.reshape(1, -1)
+    else:
+        a, ref = a.reshape(a.shape[0], -1), ref.reshape(ref.shape[0], -1)
+        slack = None if slack is None else slack.reshape(slack.shape[0], -1)
+    if a.shape[1] < NORM_MIN_ELEMS:
+        return []
+    num = torch.linalg.vector_norm(a - ref, dim=1)
+    if slack is not None:
+        num = (num - torch.linalg.vector_norm(slack, dim=1)).clamp_min(0)
+    den = torch.linalg.vector_norm(ref, dim=1)
+    return [float(n / d) if d > 0 else (0.0 if n == 0 else float("inf")) for n, d in zip(num, den)]
+
+
+def check_norm(a: torch.Tensor, ref: torch.Tensor, dtype, kind="bwd", name="", slack=None):
+    c = NORM_C[dtype]
+    rel = norm_rel_errors(a, ref, slack)
+    if not rel:
+        return None
+    worst = max(rel)
+    if worst <= c:
+        key = (str(dtype).replace("torch.", ""), kind)
+        NORM_SEEN[key] = max(NORM_SEEN.get(key, 0.0), worst)
+    else:
+        raise AssertionError(
+            f"{name}: norm-wise relative error {worst:.3g} exceeds {c:g} in head slice "
+            f"{rel.index(worst)} (||a - r||_F / ||r||_F per slice: "
+            f"{', '.join(f'{v:.2e}' for v in rel[:8])}{' ...' if len(rel) > 8 else ''})")
+    return worst
 
 
 def assert_close(a: torch.Tensor, ref: torch.Tensor, bound: torch.Tensor, dtype, kind, name=""):
@@ -107,6 +175,7 @@ def assert_close(a: torch.Tensor, ref: torch.Tensor, bound: torch.Tensor, dtype,
             f"{name}: {int(bad.sum())} of {err.numel()} elements out of tolerance; worst "
             f"got {a.flatten()[i].item():.6g} want {ref.flatten()[i].item():.6g} "
             f"(err {err.flatten()[i].item():.3g}, tol {tol.flatten()[i].item():.3g})")
+    check_norm(a, ref, dtype, kind, name, getattr(bound, "fmlp_slack", None))
 
 
 def to_np(t: torch.Tensor) -> np.ndarray:

@@ -38,3 +38,22 @@ def load_golden(name: str) -> dict:
 @pytest.fixture(scope="session")
 def golden():
     return {n: load_golden(n) for n in GOLDEN_CASES}
+
+
+def pytest_terminal_summary(terminalreporter):
+    """Largest norm-wise relative error ||a - r||_F / ||r||_F per (dtype, kind) that the
+    parity checks saw in this session, next to the bound each one is held to."""
+    try:
+        import _refcheck
+    except Exception:
+        return
+    for line in _refcheck.INFO:
+        terminalreporter.write_line(line)
+    if not _refcheck.NORM_SEEN:
+        return
+    terminalreporter.write_line("norm-wise parity (worst head slice seen / bound):")
+    for (dt, kind), v in sorted(_refcheck.NORM_SEEN.items()):
+        import torch
+
+        c = _refcheck.NORM_C[getattr(torch, dt)]
+        terminalreporter.write_line(f"  {dt:9s} {kind:4s} {v:.3e} / {c:g}")

@@ -42,7 +42,7 @@ def test_python_constants_match_header():
 def test_error_strings_and_version():
     L = _lib.lib()
     assert L.fmlp_abi_version() == 100
-    for code in range(0, 12):
+    for code in range(0, 13):
         s = L.fmlp_error_string(code).decode()
         assert s and s != "unknown error"
     assert L.fmlp_error_string(99).decode() == "unknown error"

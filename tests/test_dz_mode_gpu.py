@@ -14,7 +14,9 @@ bar as the recompute mode:
   parity tolerance, dW bit-identical when both modes split the dW programs alike;
 * with split dW programs (few heads, many B tiles) and with a shared (2-D) input;
 * at the C4 per-GPU size of 8-way head sharding against a plain PyTorch fp32 reference;
-* the workspace region past the dZ^T tiles and the outputs' neighbours are not written.
+* the workspace region past the dZ^T tiles and the outputs' neighbours are not written;
+* heads that do not fit one launch's dZ^T cap (8 GiB), or a caller's workspace limit, run
+  in head groups that reuse the workspace, with the one-launch results.
 """
 import numpy as np
 import pytest
@@ -182,10 +184,11 @@ def test_dz_mode_writes_stay_inside_their_buffers():
         assert torch.equal(b[G:-G].view_as(w), w)
 
 
-def test_dz_mode_cap_selects_recompute_above_8_gib():
-    # C4 on one GPU needs exactly 8 GiB of dZ^T (the cap: every element offset fits in 32
-    # bits); one more head does not fit, and the library asks for the recompute mode's
-    # workspace instead. Plan queries only, nothing is allocated.
+def test_dz_mode_runs_in_head_groups_above_8_gib():
+    # C4 on one GPU needs exactly 8 GiB of dZ^T (the cap of one launch: every element
+    # offset fits in 32 bits). One more head no longer falls back to the recompute mode:
+    # the heads run in two groups of 17 and 16 that reuse one workspace. Plan queries
+    # only, nothing is allocated.
     from flashmlp_b200 import _lib
 
     L = _lib.lib()
@@ -193,13 +196,50 @@ def test_dz_mode_cap_selects_recompute_above_8_gib():
     assert _plan(32, B, D, E, torch.bfloat16) == (1, 2, 3)
     assert int(L.fmlp_bwd_workspace_size(32, B, D, E, 1)) >= 8 << 30
     mode, splits, launches = _plan(33, B, D, E, torch.bfloat16)
-    assert mode == 0 and launches == 1 + (splits > 1)
-    assert int(L.fmlp_bwd_workspace_size(33, B, D, E, 1)) == int(L.fmlp_bwd_workspace_size_min(33, B, D, E, 1))
+    assert mode == 1 and launches == 2 * (2 + (splits > 1))
+    ws33 = int(L.fmlp_bwd_workspace_size(33, B, D, E, 1))
+    assert (17 << 28) <= ws33 < (8 << 30), "the workspace of the 17-head group"
+    # a smaller workspace gives smaller groups; below 4 heads' tiles, the recompute mode
+    per_head = 2 * E * B
+    mode, _, launches = _lib.bwd_plan(32, B, D, E, 1, 8 * per_head + (64 << 20))
+    assert mode == 1 and launches >= 4 * 2
+    mode, _, _ = _lib.bwd_plan(32, B, D, E, 1, 3 * per_head + (64 << 20))
+    assert mode == 0
     # below fmlp_bwd_workspace_size_min the plan (and fmlp_bwd) refuse the call
     need = int(L.fmlp_bwd_workspace_size_min(4, B, D, E, 1))
     assert need > 0
     with pytest.raises(_lib.FlashMLPError):
         _lib.bwd_plan(4, B, D, E, 1, need - 16)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_dz_mode_head_groups_match_one_launch(dt):
+    # A workspace limit that holds 4 of 6 heads' dZ tiles: the dZ-store mode runs in head
+    # groups (fmlp_bwd_plan counts their launches). dX comes from the same dZ tiles and
+    # the same GEMM per head, so it is bit-identical to the one-launch result; dW too when
+    # the groups split their dW programs as the one launch does; all of it within the
+    # parity bar of the fp32 reference.
+    from flashmlp_b200 import _lib
+
+    H, B, D, E = 6, 4096, 128, 1024
+    code = _code(dt)
+    L = _lib.lib()
+    full = int(L.fmlp_bwd_workspace_size(H, B, D, E, code))
+    limit = int(L.fmlp_bwd_workspace_size(4, B, D, E, code))
+    one = _lib.bwd_plan(H, B, D, E, code, full)
+    grouped = _lib.bwd_plan(H, B, D, E, code, limit)
+    assert one[0] == 1 and grouped[0] == 1 and grouped[2] >= 2 * one[2], (one, grouped)
+    x, w1, w2, do = make_inputs(H, B, D, E, dt, seed=77)
+    a = F().flashmlp_bwd(x, w1, w2, do, "silu")
+    with F().backward_workspace_limit(limit):
+        b = F().flashmlp_bwd(x, w1, w2, do, "silu")
+    refs = ref_bwd(x, w1, w2, do, "silu")
+    assert torch.equal(a[0], b[0]), "dX of the grouped launches differs from one launch"
+    for i, k in enumerate(("dx", "dw1", "dw2")):
+        assert_close(b[i], *refs[k], dt, "bwd", f"grouped {k}")
+        assert_close(b[i], a[i].float(), refs[k][1], dt, "bwd", f"grouped vs one launch {k}")
+    if grouped[1] == one[1]:
+        assert torch.equal(a[1], b[1]) and torch.equal(a[2], b[2])
 
 
 @pytest.mark.parametrize("shape", [(2, 300, 64, 136), (3, 1000, 128, 264), (4, 65536, 128, 2048)])

@@ -119,6 +119,7 @@ def _fused_case(rank, world):
             dist.all_gather(gathered, ws)
             ok &= all(torch.equal(gathered[0], t) for t in gathered[1:])
         ok &= not torch.equal(tr.w1, w1)
+        ok &= tr.status() == 0
         ok &= F._lib.lib().fmlp_device_status(1) == 0
         tr.close()
         results.append(bool(ok))

@@ -6,8 +6,9 @@ splits its dW programs over batch ranges. fmlp_bwd_noalloc keeps that scratch in
 device array inside the library instead. This test calls it through the C ABI on a shape
 that uses the scratch (16-bit inputs and fp32 inputs, whose TF32 dW programs split too),
 twice in a row with different inputs (the array keeps the first call's partial sums,
-which the second call must not pick up), and checks each result against fmlp_bwd's within
-the parity tolerance of the other GPU tests.
+which the second call must not pick up), and checks each result against the fp32 PyTorch
+reference with the kernels' rounding points (tests/_refcheck.py) and against fmlp_bwd's
+result, both within the parity tolerance of the other GPU tests.
 
 The file name sorts last so that a run stopping at the first failure has already run
 every other test.
@@ -46,6 +47,7 @@ def test_bwd_noalloc_matches_bwd_on_two_calls_in_a_row(dtype):
         want = F.flashmlp_bwd(x, w1, w2, do, act)  # the entry point with a caller workspace
         torch.cuda.synchronize()
         bounds = ref_bwd(x, w1, w2, do, act)
-        for name, got, ref in zip(("dx", "dw1", "dw2"), (dx, dw1, dw2), want):
-            assert_close(got, ref.float(), bounds[name][1], dt, "bwd", f"noalloc/{act}/{name}")
+        for name, got, other in zip(("dx", "dw1", "dw2"), (dx, dw1, dw2), want):
+            assert_close(got, *bounds[name], dt, "bwd", f"noalloc/{act}/{name} vs fp32 reference")
+            assert_close(got, other.float(), bounds[name][1], dt, "bwd", f"noalloc/{act}/{name} vs fmlp_bwd")
     assert L.fmlp_device_status(1) == 0
