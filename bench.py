@@ -259,10 +259,11 @@ def time_reference_triton(steps, warmup):
     hbde = float(H) * B * D * E
     torch.cuda.reset_peak_memory_stats(dev)
     before = torch.cuda.memory_allocated(dev)
-    ref.flashmlp_fwd(x, w1, w2, act)
-    ref.flashmlp_bwd(x, w1, w2, do, act)
+    o = ref.flashmlp_fwd(x, w1, w2, act)  # O stays alive through the backward, as in training
+    grads = ref.flashmlp_bwd(x, w1, w2, do, act)
     torch.cuda.synchronize()
     peak = torch.cuda.max_memory_allocated(dev) - before
+    del o, grads
     return {
         "config": WORKLOAD_NAME, "steps": steps, "autotune_and_compile_s": round(tune_s, 1),
         "fwd_ms": round(fwd, 4), "bwd_ms": round(bwd, 4), "step_ms": round(fwd + bwd, 4),
@@ -440,12 +441,15 @@ def run_ours(args, rank, world, local_rank):
         dist.all_gather(parts, t)
         return [p.tolist() for p in parts]
 
-    for _ in range(args.warmup):
-        o = F.flashmlp_fwd(x, w1, w2, act)
-        dx, dw1, dw2 = F.flashmlp_bwd(x, w1, w2, do, act)
-    # ---- parity of this rank's shard (head 0 of the full-shard launch) before timing
+    # ---- parity of this rank's shard (head 0 of the full-shard launch), before the
+    # warm-up so that the check's allocations are gone before timing
+    o = F.flashmlp_fwd(x, w1, w2, act)
+    dx, dw1, dw2 = F.flashmlp_bwd(x, w1, w2, do, act)
     ok, worst, msg = check_head0(F, x, w1, w2, do, act, o, dx, dw1, dw2)
     del o, dx, dw1, dw2
+    for _ in range(args.warmup):
+        F.flashmlp_fwd(x, w1, w2, act)
+        F.flashmlp_bwd(x, w1, w2, do, act)
     par = gather([1.0 if ok else 0.0, worst])
     parity = {"ranks_ok": int(sum(p[0] for p in par)), "ranks": world,
               "max_norm_rel_err": float(f"{max(p[1] for p in par):.3e}"),

@@ -242,7 +242,9 @@ int fwd_impl(const void* x, const void* w1, const void* w2, void* o, int H, int 
   if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(o)) return FMLP_ERR_MISALIGNED;
   FwdLaunch a{};
   a.dp = round_dp(D);
-  const int et = f32 ? 64 : fwd_et(a.dp);
+  // 64 < D <= 256 (16-bit, per-head X): CTA-pair kernel, W2 chunks of 128 E rows
+  const bool pair = !f32 && !shared_x && a.dp >= 128;
+  const int et = f32 ? 64 : (pair ? 128 : fwd_et(a.dp));
   const uint32_t inner = f32 ? 32 : 64;  // elements per 128-byte swizzled row
   // fp32: the weight chunks are read MN-major only, which needs the 32-byte-atom swizzle
   const CUtensorMapSwizzle wswz = f32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
@@ -261,7 +263,7 @@ int fwd_impl(const void* x, const void* w1, const void* w2, void* o, int H, int 
   a.sm_count = dev->sm_count;
   a.status = dev->status;
   a.stream = st;
-  return cuda_rc(f32 ? launch_fwd_tf32(a) : launch_fwd(a));
+  return cuda_rc(f32 ? launch_fwd_tf32(a) : (pair ? launch_fwd2sm(a) : launch_fwd(a)));
 }
 
 }  // namespace
