@@ -62,12 +62,11 @@ constexpr int kRows = 128;  // rows of a B tile (tcgen05 M)
 inline int fwd_et(int dp) { return dp <= 128 ? 128 : 64; }
 constexpr int kBwdEt = 128;  // E chunk of both backward program kinds
 
-int fwd_smem_bytes(int dp);
 // Forward on CTA pairs (fmlp_fwd2sm.cu): 16-bit inputs, per-head X, DP in {128, 256};
 // a.tm_w2 must have boxes of 128 E rows.
 cudaError_t launch_fwd2sm(const FwdLaunch& a);
 int bwd_smem_bytes(int dp);
-cudaError_t launch_fwd(const FwdLaunch& a);       // picks the kernel for a.dp
+cudaError_t launch_fwd(const FwdLaunch& a);       // D <= 128: the row-pair kernel
 cudaError_t launch_fwd_pair(const FwdLaunch& a);  // two row tiles per CTA, D <= 128
 cudaError_t launch_bwd(const BwdLaunch& a);     // picks the kernel for a.dp
 cudaError_t launch_bwd256(const BwdLaunch& a);  // 128 < D <= 256
