@@ -98,6 +98,57 @@ __device__ __forceinline__ uint32_t act_pair(float z0, float z1, ActState<T, ACT
   return p;
 }
 
+// What the fused dW schedule keeps per element between its two phases: the factor(s) dH
+// is multiplied by, formed from the forward state in phase 1, when the activation warps
+// would otherwise wait for dH. grad_from_fac(dh, grad_fac(st)) performs exactly the
+// operations of act_grad(dh, st) in the same order, so the results are bit-identical.
+template <typename T, int ACT>
+struct GradFac {
+  float f;  // silu: s + h (1 - s); leaky_relu: 1 or 0.01; sigmoid: the rounded h
+  float g;  // sigmoid: (1 - h) rounded to the input dtype
+};
+
+template <typename T, int ACT>
+__device__ __forceinline__ GradFac<T, ACT> grad_fac(const ActState<T, ACT>& st) {
+  if constexpr (ACT == kLeakyRelu) {
+    return {st.pos ? 1.0f : 0.01f, 0.f};
+  } else if constexpr (ACT == kSilu) {
+    return {st.s + st.hr * (1.0f - st.s), 0.f};
+  } else if constexpr (ACT == kSigmoid) {
+    return {st.hr, Pack<T>::round(1.0f - st.hr)};
+  } else {
+    return {1.0f, 0.f};
+  }
+}
+
+template <typename T, int ACT>
+__device__ __forceinline__ float grad_from_fac(float dh, const GradFac<T, ACT>& a) {
+  if constexpr (ACT == kLeakyRelu || ACT == kSilu) {
+    return dh * a.f;
+  } else if constexpr (ACT == kSigmoid) {
+    return (dh * a.f) * a.g;
+  } else {
+    return dh;
+  }
+}
+
+// Activates a pair (packed rounded H returned) and records the factors dH is multiplied by.
+template <typename T, int ACT>
+__device__ __forceinline__ uint32_t act_pair_fac(float z0, float z1, GradFac<T, ACT>& a0, GradFac<T, ACT>& a1) {
+  ActState<T, ACT> s0, s1;
+  const uint32_t p = act_pair<T, ACT>(z0, z1, s0, s1);
+  a0 = grad_fac<T, ACT>(s0);
+  a1 = grad_fac<T, ACT>(s1);
+  return p;
+}
+
+// dz = dh * act'(z) for a pair from the recorded factors, rounded and packed.
+template <typename T, int ACT>
+__device__ __forceinline__ uint32_t grad_pair_fac(float dh0, float dh1, const GradFac<T, ACT>& a0,
+                                                  const GradFac<T, ACT>& a1) {
+  return Pack<T>::pack(grad_from_fac<T, ACT>(dh0, a0), grad_from_fac<T, ACT>(dh1, a1));
+}
+
 // dz = dh * act'(z) for a pair, rounded and packed.
 template <typename T, int ACT>
 __device__ __forceinline__ uint32_t grad_pair(float dh0, float dh1, const ActState<T, ACT>& s0,

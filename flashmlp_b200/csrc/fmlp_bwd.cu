@@ -39,10 +39,11 @@
 //   dW1^T  += dZ^T(i)[tmem] @ X_i[smem]   TS M=128(e) N=DP     K=128(b)
 // X and dO tiles stream through separate 2-stage rings: dW2(i) frees dO_i, dW1^T(i) frees
 // X_i, so X_{i+1} lands while phase 2(i) runs.
-// Fused-phase schedule (bf16 silu): the activation warps load Z^T(i) into registers and
-// release its columns at once (z_free), so Z^T(i+1) is computed while they are still on
-// the SFU; after loading dH^T(i) they pack H^T(i) into the first 16 and dZ^T(i) into the
-// last 16 columns of each 32-column dH^T slice. Issue order: after z_free(i): Z^T(i+1);
+// Fused-phase schedule (every activation but sigmoid): the activation warps load Z^T(i)
+// into registers and release its columns at once (z_free), so Z^T(i+1) is computed while
+// they are still on the SFU, where they also form the factor dH is multiplied by; after
+// loading dH^T(i) they pack H^T(i) into the first 16 and dZ^T(i) into the last 16
+// columns of each 32-column dH^T slice. Issue order: after z_free(i): Z^T(i+1);
 // after both are packed: dW2(i) dW1^T(i) dH^T(i+1). X_{i+1} is read before dW1^T(i) frees
 // X_i, so the X ring has 3 stages in this schedule.
 //
@@ -120,9 +121,11 @@ __global__ void __launch_bounds__(576, 1)
   using St = ActState<T, ACT>;
   constexpr int BM = C::BM;
   constexpr int NACT = C::NUM_ACT_WARPS;
-  // dW programs of bf16 silu run the fused-phase schedule (see the dW notes; measured
-  // 1.9 % faster for C4 silu, 3.3 % slower for sigmoid; the fp16 variant would spill)
-  constexpr bool kFused = ACT == kSilu && Pack<T>::kBF16;
+  // dW programs run the fused-phase schedule (see the dW notes) for every activation but
+  // sigmoid, whose two recorded factors per element make it spill and measured 5-10 %
+  // slower (C4 silu bf16 -2 % against the two-phase schedule, fp16 -3 %, leaky_relu and
+  // linear -2 to -3 %)
+  constexpr bool kFused = ACT != kSigmoid;
   constexpr bool kBF = Pack<T>::kBF16;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -419,7 +422,10 @@ __global__ void __launch_bounds__(576, 1)
       auto dz_at = [&](int bt) -> T* { return dzt == nullptr ? nullptr : dzt + (dz_off + uint32_t(bt) * (BM * 128)); };
       bool ok = true;
       for (int bt = 0; bt < nT && ok && kFused; ++bt) {
-        St st[32];
+        // Phase 1 also forms the factors dH is multiplied by (grad_fac), while dH^T(bt)
+        // is still being computed, so phase 2 -- on the path to the next dH^T -- is one
+        // or two multiplies per element.
+        GradFac<T, ACT> fac[32];
         uint32_t hp[16];
         if (!(ok = mbar_wait(&p_full[0], bt & 1, ctx))) break;
         tc_fence_after();
@@ -431,30 +437,32 @@ __global__ void __launch_bounds__(576, 1)
           signal(z_free, false);  // Z^T(bt) is in registers: Z^T(bt+1) may overwrite it
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            hp[i] = act_pair<T, ACT>(__uint_as_float(va[2 * i]), __uint_as_float(va[2 * i + 1]), st[2 * i], st[2 * i + 1]);
+            hp[i] = act_pair_fac<T, ACT>(__uint_as_float(va[2 * i]), __uint_as_float(va[2 * i + 1]), fac[2 * i],
+                                         fac[2 * i + 1]);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            hp[8 + i] = act_pair<T, ACT>(__uint_as_float(vb[2 * i]), __uint_as_float(vb[2 * i + 1]), st[16 + 2 * i],
-                                         st[17 + 2 * i]);
+            hp[8 + i] = act_pair_fac<T, ACT>(__uint_as_float(vb[2 * i]), __uint_as_float(vb[2 * i + 1]), fac[16 + 2 * i],
+                                             fac[17 + 2 * i]);
         }
         if (!(ok = mbar_wait(&p_full[1], bt & 1, ctx))) break;
         tc_fence_after();
         {
-          // dH^T columns [0,16) of this slice -> registers, then H^T packed over them;
-          // columns [16,32) -> registers, then dZ^T packed over them
-          uint32_t v[16], pd[8];
+          // dH^T columns [0,32) of this slice -> registers (one wait); H^T packed over
+          // columns [0,16), dZ^T over [16,32)
+          uint32_t va[16], vb[16], pd[8];
           T* g = dz_at(bt);
-          tmem_ld16_sync(dt, v);
+          tmem_ld16_async(dt, va);
+          tmem_ld16_async(dt + 16, vb);
+          tmem_wait_ld_dep2(va, vb);
           tmem_st16(dt, hp);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            pd[i] = grad_pair<T, ACT>(dh_in(v[2 * i]), dh_in(v[2 * i + 1]), st[2 * i], st[2 * i + 1]);
-          tmem_ld16_sync(dt + 16, v);
+            pd[i] = grad_pair_fac<T, ACT>(dh_in(va[2 * i]), dh_in(va[2 * i + 1]), fac[2 * i], fac[2 * i + 1]);
           tmem_st8(dt + 16, pd);
           if (g != nullptr) store_dz(g, pd);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            pd[i] = grad_pair<T, ACT>(dh_in(v[2 * i]), dh_in(v[2 * i + 1]), st[16 + 2 * i], st[17 + 2 * i]);
+            pd[i] = grad_pair_fac<T, ACT>(dh_in(vb[2 * i]), dh_in(vb[2 * i + 1]), fac[16 + 2 * i], fac[17 + 2 * i]);
           tmem_st8(dt + 24, pd);
           if (g != nullptr) store_dz(g + 1024, pd);
         }
