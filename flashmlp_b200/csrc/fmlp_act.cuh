@@ -72,20 +72,26 @@ __device__ __forceinline__ float act_grad(float dh, const ActState<T, ACT>& st) 
 // derivative state; the rounded H is read back from the packed word with integer ops.
 template <typename T, int ACT>
 __device__ __forceinline__ uint32_t act_pair(float z0, float z1, ActState<T, ACT>& s0, ActState<T, ACT>& s1) {
+  // the scalar operations of sigmoid_fast and act_forward, two elements per instruction
   float h0, h1;
   if constexpr (ACT == kLeakyRelu) {
     s0.pos = z0 >= 0.f;
     s1.pos = z1 >= 0.f;
-    h0 = fmaxf(z0, 0.01f * z0);
-    h1 = fmaxf(z1, 0.01f * z1);
+    const uint64_t m = mul2(f2(0.01f, 0.01f), f2(z0, z1));
+    h0 = fmaxf(z0, f2_lo(m));
+    h1 = fmaxf(z1, f2_hi(m));
   } else if constexpr (ACT == kSilu) {
-    s0.s = sigmoid_fast(z0);
-    s1.s = sigmoid_fast(z1);
-    h0 = z0 * s0.s;
-    h1 = z1 * s1.s;
+    const uint64_t half = f2(0.5f, 0.5f), z = f2(z0, z1);
+    const uint64_t u = mul2(half, z);
+    const uint64_t sg = fma2(half, f2(tanh_approx(f2_lo(u)), tanh_approx(f2_hi(u))), half);
+    const uint64_t h = mul2(z, sg);
+    s0.s = f2_lo(sg), s1.s = f2_hi(sg);
+    h0 = f2_lo(h), h1 = f2_hi(h);
   } else if constexpr (ACT == kSigmoid) {
-    h0 = sigmoid_fast(z0);
-    h1 = sigmoid_fast(z1);
+    const uint64_t half = f2(0.5f, 0.5f);
+    const uint64_t u = mul2(half, f2(z0, z1));
+    const uint64_t sg = fma2(half, f2(tanh_approx(f2_lo(u)), tanh_approx(f2_hi(u))), half);
+    h0 = f2_lo(sg), h1 = f2_hi(sg);
   } else {
     h0 = z0;
     h1 = z1;
@@ -137,8 +143,15 @@ template <typename T, int ACT>
 __device__ __forceinline__ uint32_t act_pair_fac(float z0, float z1, GradFac<T, ACT>& a0, GradFac<T, ACT>& a1) {
   ActState<T, ACT> s0, s1;
   const uint32_t p = act_pair<T, ACT>(z0, z1, s0, s1);
-  a0 = grad_fac<T, ACT>(s0);
-  a1 = grad_fac<T, ACT>(s1);
+  if constexpr (ACT == kSilu) {  // grad_fac's s + h (1 - s), two elements per instruction
+    const uint64_t sg = f2(s0.s, s1.s);
+    const uint64_t f = fma2(f2(s0.hr, s1.hr), sub2(f2(1.0f, 1.0f), sg), sg);
+    a0.f = f2_lo(f), a1.f = f2_hi(f);
+    a0.g = a1.g = 0.f;
+  } else {
+    a0 = grad_fac<T, ACT>(s0);
+    a1 = grad_fac<T, ACT>(s1);
+  }
   return p;
 }
 
@@ -146,22 +159,61 @@ __device__ __forceinline__ uint32_t act_pair_fac(float z0, float z1, GradFac<T, 
 template <typename T, int ACT>
 __device__ __forceinline__ uint32_t grad_pair_fac(float dh0, float dh1, const GradFac<T, ACT>& a0,
                                                   const GradFac<T, ACT>& a1) {
-  return Pack<T>::pack(grad_from_fac<T, ACT>(dh0, a0), grad_from_fac<T, ACT>(dh1, a1));
+  if constexpr (ACT == kLeakyRelu || ACT == kSilu) {  // grad_from_fac, two elements per instruction
+    const uint64_t d = mul2(f2(dh0, dh1), f2(a0.f, a1.f));
+    return Pack<T>::pack(f2_lo(d), f2_hi(d));
+  } else if constexpr (ACT == kSigmoid) {
+    const uint64_t d = mul2(mul2(f2(dh0, dh1), f2(a0.f, a1.f)), f2(a0.g, a1.g));
+    return Pack<T>::pack(f2_lo(d), f2_hi(d));
+  } else {
+    return Pack<T>::pack(grad_from_fac<T, ACT>(dh0, a0), grad_from_fac<T, ACT>(dh1, a1));
+  }
 }
 
 // dz = dh * act'(z) for a pair, rounded and packed.
 template <typename T, int ACT>
 __device__ __forceinline__ uint32_t grad_pair(float dh0, float dh1, const ActState<T, ACT>& s0,
                                               const ActState<T, ACT>& s1) {
-  return Pack<T>::pack(act_grad<T, ACT>(dh0, s0), act_grad<T, ACT>(dh1, s1));
+  if constexpr (ACT == kSilu) {  // act_grad's dh (s + h (1 - s)), two elements per instruction
+    const uint64_t sg = f2(s0.s, s1.s);
+    const uint64_t f = fma2(f2(s0.hr, s1.hr), sub2(f2(1.0f, 1.0f), sg), sg);
+    const uint64_t d = mul2(f2(dh0, dh1), f);
+    return Pack<T>::pack(f2_lo(d), f2_hi(d));
+  } else if constexpr (ACT == kSigmoid) {  // (dh h) round(1 - h)
+    const uint64_t hr = f2(s0.hr, s1.hr);
+    const uint64_t om = sub2(f2(1.0f, 1.0f), hr);
+    const uint64_t d = mul2(mul2(f2(dh0, dh1), hr), f2(Pack<T>::round(f2_lo(om)), Pack<T>::round(f2_hi(om))));
+    return Pack<T>::pack(f2_lo(d), f2_hi(d));
+  } else if constexpr (ACT == kLeakyRelu) {
+    const uint64_t d = mul2(f2(dh0, dh1), f2(s0.pos ? 1.0f : 0.01f, s1.pos ? 1.0f : 0.01f));
+    return Pack<T>::pack(f2_lo(d), f2_hi(d));
+  } else {
+    return Pack<T>::pack(act_grad<T, ACT>(dh0, s0), act_grad<T, ACT>(dh1, s1));
+  }
 }
 
 // Packs 2*N fp32 values (activated) into N 16-bit pairs.
 template <typename T, int ACT, int N>
 __device__ __forceinline__ void act_pack(const uint32_t* v, uint32_t* p) {
 #pragma unroll
-  for (int i = 0; i < N; ++i)
-    p[i] = Pack<T>::pack(act_fwd<T, ACT>(__uint_as_float(v[2 * i])), act_fwd<T, ACT>(__uint_as_float(v[2 * i + 1])));
+  for (int i = 0; i < N; ++i) {
+    const float z0 = __uint_as_float(v[2 * i]), z1 = __uint_as_float(v[2 * i + 1]);
+    if constexpr (ACT == kSilu) {  // act_fwd's u tanh(u) + u, two elements per instruction
+      const uint64_t u = mul2(f2(0.5f, 0.5f), f2(z0, z1));
+      const uint64_t h = fma2(u, f2(tanh_approx(f2_lo(u)), tanh_approx(f2_hi(u))), u);
+      p[i] = Pack<T>::pack(f2_lo(h), f2_hi(h));
+    } else if constexpr (ACT == kSigmoid) {
+      const uint64_t half = f2(0.5f, 0.5f);
+      const uint64_t u = mul2(half, f2(z0, z1));
+      const uint64_t h = fma2(half, f2(tanh_approx(f2_lo(u)), tanh_approx(f2_hi(u))), half);
+      p[i] = Pack<T>::pack(f2_lo(h), f2_hi(h));
+    } else if constexpr (ACT == kLeakyRelu) {
+      const uint64_t m = mul2(f2(0.01f, 0.01f), f2(z0, z1));
+      p[i] = Pack<T>::pack(fmaxf(z0, f2_lo(m)), fmaxf(z1, f2_hi(m)));
+    } else {
+      p[i] = Pack<T>::pack(z0, z1);
+    }
+  }
 }
 
 // Packs 2*N fp32 values unchanged.
