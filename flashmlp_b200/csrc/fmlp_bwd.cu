@@ -242,11 +242,18 @@ __global__ void __launch_bounds__(576, 1)
     if constexpr (SX) return __uint_as_float(v) * inv_h;
     return __uint_as_float(v);
   };
+  auto signal = [&](uint64_t* bar, bool wrote_tmem) {
+    if (wrote_tmem) tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+  };
   // Phase 2 over the 32 dH columns at `src`: dZ packed into the 16 columns at `dst`
-  // (`dst` == `src`, or columns this warp has already read in phase 1), and, if `g` is
-  // set, the same 32 16-bit values stored to the dZ-store workspace at g.
-  auto phase2 = [&](uint32_t src, uint32_t dst, const St (&st)[32], T* g) {
-    uint32_t va[16], vb[16], pd[8];
+  // (`dst` == `src`, or columns this warp has already read in phase 1), `done` signalled
+  // once they are in TMEM, and then, if `g` is set, the same 32 16-bit values stored to
+  // the dZ-store workspace at g (off the chain of the products waiting on `done`).
+  auto phase2 = [&](uint32_t src, uint32_t dst, const St (&st)[32], T* g, uint64_t* done) {
+    uint32_t va[16], vb[16], pd[8], pe[8];
     tmem_ld16_async(src, va);
     tmem_wait_ld_dep(va);
     tmem_ld16_async(src + 16, vb);
@@ -254,20 +261,17 @@ __global__ void __launch_bounds__(576, 1)
     for (int i = 0; i < 8; ++i)
       pd[i] = grad_pair<T, ACT>(dh_in(va[2 * i]), dh_in(va[2 * i + 1]), st[2 * i], st[2 * i + 1]);
     tmem_st8(dst, pd);
-    if (g != nullptr) store_dz(g, pd);
     tmem_wait_ld_dep(vb);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      pd[i] = grad_pair<T, ACT>(dh_in(vb[2 * i]), dh_in(vb[2 * i + 1]), st[16 + 2 * i],
+      pe[i] = grad_pair<T, ACT>(dh_in(vb[2 * i]), dh_in(vb[2 * i + 1]), st[16 + 2 * i],
                                 st[17 + 2 * i]);
-    tmem_st8(dst + 8, pd);
-    if (g != nullptr) store_dz(g + 1024, pd);
-  };
-  auto signal = [&](uint64_t* bar, bool wrote_tmem) {
-    if (wrote_tmem) tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar);
+    tmem_st8(dst + 8, pe);
+    signal(done, true);
+    if (g != nullptr) {
+      store_dz(g, pd);
+      store_dz(g + 1024, pe);
+    }
   };
 
   // Packed operands with K = 128 rows/columns: the 16-bit values of columns [16k, 16k+16)
@@ -449,7 +453,9 @@ __global__ void __launch_bounds__(576, 1)
         {
           // dH^T columns [0,32) of this slice -> registers (one wait); H^T packed over
           // columns [0,16), dZ^T over [16,32)
-          uint32_t va[16], vb[16], pd[8];
+          // The dZ-store writes follow the signal: the dW products and dH^T(bt+1) need
+          // only the TMEM copy, so the global stores stay off their chain.
+          uint32_t va[16], vb[16], pd[8], pe[8];
           T* g = dz_at(bt);
           tmem_ld16_async(dt, va);
           tmem_ld16_async(dt + 16, vb);
@@ -459,14 +465,16 @@ __global__ void __launch_bounds__(576, 1)
           for (int i = 0; i < 8; ++i)
             pd[i] = grad_pair_fac<T, ACT>(dh_in(va[2 * i]), dh_in(va[2 * i + 1]), fac[2 * i], fac[2 * i + 1]);
           tmem_st8(dt + 16, pd);
-          if (g != nullptr) store_dz(g, pd);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            pd[i] = grad_pair_fac<T, ACT>(dh_in(vb[2 * i]), dh_in(vb[2 * i + 1]), fac[16 + 2 * i], fac[17 + 2 * i]);
-          tmem_st8(dt + 24, pd);
-          if (g != nullptr) store_dz(g + 1024, pd);
+            pe[i] = grad_pair_fac<T, ACT>(dh_in(vb[2 * i]), dh_in(vb[2 * i + 1]), fac[16 + 2 * i], fac[17 + 2 * i]);
+          tmem_st8(dt + 24, pe);
+          signal(&a_full[1], true);
+          if (g != nullptr) {
+            store_dz(g, pd);
+            store_dz(g + 1024, pe);
+          }
         }
-        signal(&a_full[1], true);
       }
       for (int bt = 0; bt < nT && ok && !kFused; ++bt) {
         St st[32];
@@ -476,8 +484,7 @@ __global__ void __launch_bounds__(576, 1)
         signal(&a_full[0], true);
         if (!(ok = mbar_wait(&p_full[1], bt & 1, ctx))) break;
         tc_fence_after();
-        phase2(dt, dt, st, dz_at(bt));  // dZ^T packed over dH^T
-        signal(&a_full[1], true);
+        phase2(dt, dt, st, dz_at(bt), &a_full[1]);  // dZ^T packed over dH^T
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
         tc_fence_after();
@@ -691,8 +698,7 @@ __global__ void __launch_bounds__(576, 1)
         phase1(zc, st, false);  // derivative state only
         if (!(ok = mbar_wait(&p_full[1], c & 1, ctx))) break;
         tc_fence_after();
-        phase2(da, zc, st, nullptr);  // dZ packed over this warp's Z columns
-        signal(&a_full[1], true);
+        phase2(da, zc, st, nullptr, &a_full[1]);  // dZ packed over this warp's Z columns
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
         tc_fence_after();

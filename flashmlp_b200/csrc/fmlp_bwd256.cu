@@ -177,25 +177,27 @@ __global__ void __launch_bounds__(576, 1)
       p[i] = act_pair<T, ACT>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]), st[2 * i], st[2 * i + 1]);
     if (pack_h) tmem_st8(col, p);
   };
-  // Phase 2 over the 16 dH columns at `col`: dZ packed into the first 8 of them and, if
-  // `g` is set, stored to the dZ-store workspace as two 8-value pieces at g and g + 512.
-  auto phase2 = [&](uint32_t col, const St (&st)[16], T* gz) {
+  auto signal = [&](uint64_t* bar, bool wrote_tmem) {
+    if (wrote_tmem) tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+  };
+  // Phase 2 over the 16 dH columns at `col`: dZ packed into the first 8 of them, `done`
+  // signalled, and then, if `gz` is set, the values stored to the dZ-store workspace as
+  // two 8-value pieces at gz and gz + 512 (off the chain of the products waiting on `done`).
+  auto phase2 = [&](uint32_t col, const St (&st)[16], T* gz, uint64_t* done) {
     uint32_t v[16], p[8];
     tmem_ld16_sync(col, v);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       p[i] = grad_pair<T, ACT>(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]), st[2 * i], st[2 * i + 1]);
     tmem_st8(col, p);
+    signal(done, true);
     if (gz != nullptr) {
       *reinterpret_cast<uint4*>(gz) = make_uint4(p[0], p[1], p[2], p[3]);
       *reinterpret_cast<uint4*>(gz + 512) = make_uint4(p[4], p[5], p[6], p[7]);
     }
-  };
-  auto signal = [&](uint64_t* bar, bool wrote_tmem) {
-    if (wrote_tmem) tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar);
   };
   // Packed operand with K = 64: the 16-bit values of K-step k sit in the first 8 columns
   // of 16-column slice k.
@@ -353,8 +355,8 @@ __global__ void __launch_bounds__(576, 1)
         signal(&a_full[0], true);
         if (!(ok = mbar_wait(&p_full[1], t & 1, ctx))) break;
         tc_fence_after();
-        phase2(dt, st, dz != nullptr ? dz + (dz_off + uint32_t(t >> 1) * (BM * 128) + uint32_t(t & 1) * 4096) : nullptr);
-        signal(&a_full[1], true);
+        phase2(dt, st, dz != nullptr ? dz + (dz_off + uint32_t(t >> 1) * (BM * 128) + uint32_t(t & 1) * 4096) : nullptr,
+               &a_full[1]);
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
         tc_fence_after();
@@ -559,8 +561,7 @@ __global__ void __launch_bounds__(576, 1)
         signal(&a_full[0], false);
         if (!(ok = mbar_wait(&p_full[1], c & 1, ctx))) break;
         tc_fence_after();
-        phase2(da, st, nullptr);  // dZ packed over dH
-        signal(&a_full[1], true);
+        phase2(da, st, nullptr, &a_full[1]);  // dZ packed over dH
       }
       if (ok && (ok = mbar_wait(acc_full, 0, ctx))) {
         tc_fence_after();
