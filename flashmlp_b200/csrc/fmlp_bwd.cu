@@ -778,13 +778,22 @@ static cudaError_t launch_bwd_sx(const BwdLaunch& a) {
   cudaError_t le = cudaGetLastError();
   if (le == cudaSuccess && dz) le = launch_dx_gemm(a);
   if (le != cudaSuccess || splits == 1) return le;
+  return launch_dw_reduce(a);
+}
+
+template <typename T>
+static cudaError_t launch_dw_reduce_t(const BwdLaunch& a) {
   const long long n4 = (long long)a.H * a.D * a.E / 4;  // E % 8 == 0
   long long blocks = (n4 + 255) / 256;
   const long long cap = (long long)a.sm_count * 4;
   if (blocks > cap) blocks = cap;
   fmlp_dw_reduce_kernel<T><<<dim3(unsigned(blocks), 2), 256, 0, a.stream>>>(
-      a.part, reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), a.dw_f32, n4, splits);
+      a.part, reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), a.dw_f32, n4, a.splits);
   return cudaGetLastError();
+}
+
+cudaError_t launch_dw_reduce(const BwdLaunch& a) {
+  return a.bf16 ? launch_dw_reduce_t<__nv_bfloat16>(a) : launch_dw_reduce_t<__half>(a);
 }
 
 template <int DP, typename T, int ACT>
@@ -835,20 +844,24 @@ size_t bwd_dz_bytes(int H, int B, int D, int E, int sm_count, int elem_bytes) {
 }
 
 int bwd_dz_splits(int H, int B, int D, int E, int sm_count) {
-  if (D > 128 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 1;
+  if (D > 256 || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 1;
   const long long nB = (B + kRows - 1) / kRows, nE = (E + kBwdEt - 1) / kBwdEt;
   // The launch holds dW programs only, all of the same length, so it runs in whole waves
   // of sm_count programs: pick S (1..16, at least 2 B tiles per split) minimising
   // waves * (tiles per program + 2 for a program's fill and drain) * tile time + the fp32
-  // reduce of the partials (S > 1).
-  const int dp = D <= 64 ? 64 : 128;
-  const double tile_s = 8.0 * 128 * 128 * dp / (1.2e15 / sm_count);  // 4 products of 128x128xDP
+  // reduce of the partials (S > 1). For 128 < D <= 256 (fmlp_bwd256.cu) there are two
+  // programs per (head, E chunk), one per D half, each forming Z^T and dH^T over all of D.
+  const int dp = D <= 64 ? 64 : (D <= 128 ? 128 : 256);
+  const int per_chunk = dp == 256 ? 2 : 1;
+  const double tile_flop = dp == 256 ? 4.0 * 128 * 128 * 256 + 4.0 * 128 * 128 * 128  // Z^T, dH^T, two half dW
+                                     : 8.0 * 128 * 128 * dp;                          // 4 products of 128x128xDP
+  const double tile_s = tile_flop / (1.2e15 / sm_count);
   const double hde = double(H) * D * E;
   const long long max_s = nB / 2 < 16 ? nB / 2 : 16;
   int best = 1;
   double best_t = 0;
   for (long long s = 1; s <= (max_s < 1 ? 1 : max_s); ++s) {
-    const long long progs = (long long)H * nE * s;
+    const long long progs = (long long)H * nE * s * per_chunk;
     const long long waves = (progs + sm_count - 1) / sm_count;
     double t = double(waves) * double((nB + s - 1) / s + 2) * tile_s;
     if (s > 1) t += (8.0 * s + 4.0) * hde / 6.0e12 + 5e-6;

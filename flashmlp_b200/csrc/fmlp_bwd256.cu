@@ -85,8 +85,8 @@ __global__ void __launch_bounds__(576, 1)
                        const __grid_constant__ CUtensorMap tm_w1,
                        const __grid_constant__ CUtensorMap tm_w2, const T* __restrict__ X,
                        const T* __restrict__ W1, T* __restrict__ dX, T* __restrict__ dW1,
-                       T* __restrict__ dW2, float* __restrict__ dwf, T* __restrict__ dzt, int H, int B,
-                       int D, int E, uint32_t* status) {
+                       T* __restrict__ dW2, float* __restrict__ dwf, float* __restrict__ part,
+                       T* __restrict__ dzt, int splits, int H, int B, int D, int E, uint32_t* status) {
   using C = Bwd256Cfg;
   using St = ActState<T, ACT>;
   constexpr int DP = C::DP;
@@ -104,17 +104,19 @@ __global__ void __launch_bounds__(576, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int nEw = (E + C::EW - 1) / C::EW;  // dW programs per head and D half
-  const bool is_dw = int(blockIdx.x) < H * nEw * 2;
-  int h, idx, g = 0;
-  if (is_dw) {
-    h = blockIdx.x / (nEw * 2);
-    const int r = blockIdx.x % (nEw * 2);
-    idx = r >> 1;  // E chunk
-    g = r & 1;     // D half
+  const int nEw = (E + C::EW - 1) / C::EW;  // dW programs per head, D half and B range
+  const int nW = H * nEw * 2 * splits;
+  const bool is_dw = int(blockIdx.x) < nW;
+  int h, idx, g = 0, split = 0;
+  if (is_dw) {  // (head, B range, E chunk, D half), D half fastest
+    h = blockIdx.x / (nEw * 2 * splits);
+    const int r = blockIdx.x % (nEw * 2 * splits);
+    split = r / (nEw * 2);
+    idx = (r % (nEw * 2)) >> 1;  // E chunk
+    g = r & 1;                   // D half
   } else {
     const int nBx = (B + BM - 1) / BM;
-    const int p = blockIdx.x - H * nEw * 2;
+    const int p = blockIdx.x - nW;
     h = p / nBx;
     idx = p % nBx;  // B tile
   }
@@ -206,7 +208,13 @@ __global__ void __launch_bounds__(576, 1)
   if (is_dw) {
     // ==================================================================== dW program
     const int c = idx;
-    const int nT = (B + C::BT - 1) / C::BT;
+    // this program's 64-row tiles [t0, t0 + nT): the 128-row B tiles of its range
+    const int nB128 = (B + BM - 1) / BM;
+    const int bt0 = int((long long)split * nB128 / splits);
+    const int bt1 = int((long long)(split + 1) * nB128 / splits);
+    const int t0 = 2 * bt0;
+    const int nT64 = (B + C::BT - 1) / C::BT;
+    const int nT = (2 * bt1 < nT64 ? 2 * bt1 : nT64) - t0;
     uint8_t* sW2 = smem + C::W_OFF_W2;
     uint8_t* sX = smem + C::W_OFF_X;
     uint8_t* sDO = smem + C::W_OFF_DO;
@@ -224,12 +232,12 @@ __global__ void __launch_bounds__(576, 1)
           if (!mbar_wait(&ring_empty[s], par, ctx)) break;
           mbar_arrive_expect_tx(&ring_full[s], C::WT_BYTES);
           for (int r = 0; r < 4; ++r)
-            tma_load_3d(sX + s * C::WT_BYTES + r * (C::BT * 128), &tm_x, &ring_full[s], 64 * r, t * C::BT, h);
+            tma_load_3d(sX + s * C::WT_BYTES + r * (C::BT * 128), &tm_x, &ring_full[s], 64 * r, (t0 + t) * C::BT, h);
           ++nx;
           if (!mbar_wait(&w2_empty[s], par, ctx)) break;
           mbar_arrive_expect_tx(&w2_full[s], C::WT_BYTES);
           for (int r = 0; r < 4; ++r)
-            tma_load_3d(sDO + s * C::WT_BYTES + r * (C::BT * 128), &tm_do, &w2_full[s], 64 * r, t * C::BT, h);
+            tma_load_3d(sDO + s * C::WT_BYTES + r * (C::BT * 128), &tm_do, &w2_full[s], 64 * r, (t0 + t) * C::BT, h);
           ++nd;
         }
         mbar_wait(in_full, 0, drain);
@@ -342,8 +350,7 @@ __global__ void __launch_bounds__(576, 1)
       // B tile t / 2; this thread (e = 32q + lane) owns b = 64(t%2) + 16j + 0..15: 8-b
       // groups 8(t%2) + 2j and the next. 32-bit element offsets (the workspace holds at
       // most 2^32 elements).
-      const int nB128 = (B + BM - 1) / BM;
-      const uint32_t dz_off = uint32_t((size_t(h) * nEw + c) * nB128 * (BM * 128)) + (q >> 1) * 8192 +
+      const uint32_t dz_off = uint32_t(((size_t(h) * nEw + c) * nB128 + bt0) * (BM * 128)) + (q >> 1) * 8192 +
                               (2 * j) * 512 + ((q & 1) * 32 + lane) * 8;
       T* const dz = (g == 0) ? dzt : nullptr;
       bool ok = true;
@@ -362,10 +369,13 @@ __global__ void __launch_bounds__(576, 1)
         tc_fence_after();
         const int e = c * C::EW + q * 32 + lane;
         const int d0 = g * 128 + 32 * j;  // this warp's 32 accumulator columns
-        if (dwf != nullptr) {
-          // unrounded fp32 output: dW1 laid out (H, D, E), then dW2 laid out (H, E, D)
-          float* f1 = dwf;
-          float* f2 = dwf + size_t(H) * D * E;
+        // fp32 sums: this B range's partials (fmlp_dw_reduce_kernel adds the ranges in
+        // order), or the unrounded fp32 output
+        float* fout = part != nullptr ? part + size_t(split) * 2 * (size_t(H) * D * E) : dwf;
+        if (fout != nullptr) {
+          // dW1 laid out (H, D, E), then dW2 laid out (H, E, D)
+          float* f1 = fout;
+          float* f2 = fout + size_t(H) * D * E;
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             uint32_t v[16];
@@ -598,15 +608,20 @@ static cudaError_t launch_bwd256_t(const BwdLaunch& a) {
   const int nEw = (a.E + C::EW - 1) / C::EW;
   // dZ-store mode: dW programs only (they store dZ^T), then fmlp_dx_gemm_kernel forms dX
   const bool dz = a.dzt != nullptr;
-  const long long grid = (long long)a.H * (2LL * nEw + (dz ? 0 : nBx));
+  // dW programs over `splits` B ranges (fp32 partials reduced afterwards) when there are
+  // too few (head, E chunk, D half) programs for the SMs
+  const int splits = a.splits < 1 ? 1 : a.splits;
+  if (splits > 1 && (a.part == nullptr || splits > nBx)) return cudaErrorInvalidValue;
+  const long long grid = (long long)a.H * (2LL * nEw * splits + (dz ? 0 : nBx));
   if (grid <= 0 || grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   kern<<<unsigned(grid), C::NUM_THREADS, C::SMEM, a.stream>>>(
       a.tm_x, a.tm_do, a.tm_w1, a.tm_w2, reinterpret_cast<const T*>(a.x), reinterpret_cast<const T*>(a.w1),
       reinterpret_cast<T*>(a.dx), reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), a.dw_f32,
-      reinterpret_cast<T*>(a.dzt), a.H, a.B, a.D, a.E, a.status);
+      splits > 1 ? a.part : nullptr, reinterpret_cast<T*>(a.dzt), splits, a.H, a.B, a.D, a.E, a.status);
   cudaError_t le = cudaGetLastError();
   if (le == cudaSuccess && dz) le = launch_dx_gemm(a);
-  return le;
+  if (le != cudaSuccess || splits == 1) return le;
+  return launch_dw_reduce(a);
 }
 
 template <typename T>

@@ -71,6 +71,8 @@ cudaError_t launch_fwd_pair(const FwdLaunch& a);  // two row tiles per CTA, D <=
 cudaError_t launch_bwd(const BwdLaunch& a);     // picks the kernel for a.dp
 cudaError_t launch_bwd256(const BwdLaunch& a);  // 128 < D <= 256
 cudaError_t launch_dx_gemm(const BwdLaunch& a);  // dX from the stored dZ^T (dZ-store mode)
+// fixed-order sum of the a.splits fp32 dW partials at a.part into dw1/dw2 (or a.dw_f32)
+cudaError_t launch_dw_reduce(const BwdLaunch& a);
 cudaError_t launch_fwd_tf32(const FwdLaunch& a);  // fp32 inputs, TF32 products, D <= 128
 cudaError_t launch_bwd_tf32(const BwdLaunch& a);
 int bwd256_smem_bytes();
