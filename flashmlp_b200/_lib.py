@@ -25,13 +25,14 @@ FMLP_ERR_UNSUPPORTED_E = 4
 FMLP_ERR_DEVICE_TIMEOUT = 10
 FMLP_ERR_SCRATCH_LIMIT = 11
 FMLP_ERR_PEER_ABORT = 12
+FMLP_ERR_INVALID_SCALE = 13
 FMLP_MAX_PEERS = 8
 FMLP_PEER_FLAG_WORDS = 32   # uint32 words of each rank's flag array
 FMLP_PEER_STATUS_WORD = 16  # this rank's call status in its own flag array
 FMLP_IPC_HANDLE_BYTES = 64
 
 # Every symbol the header declares, with (restype, argtypes).
-_c_int, _c_vp, _c_sz = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
+_c_int, _c_vp, _c_sz, _c_float = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float
 _c_ip = ctypes.POINTER(ctypes.c_int)
 SIGNATURES = {
     "fmlp_fwd": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp]),
@@ -49,6 +50,11 @@ SIGNATURES = {
          _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp],
     ),
     "fmlp_fwd_shared_x": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_vp]),
+    "fmlp_fwd_fp8": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int,
+         _c_float, _c_float, _c_float, _c_float, _c_int, _c_int, _c_vp],
+    ),
     "fmlp_bwd_shared_x": (
         _c_int,
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_sz,

@@ -108,6 +108,18 @@ int encode3d(CUtensorMap* m, const void* ptr, int dtype, uint64_t d0, uint64_t d
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// 3-D map of a byte tensor (e4m3 values) {d0, d1, d2} with 128 x 128-byte boxes.
+int encode3d_u8(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2) {
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0, d0 * d1};
+  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FMLP_OK : FMLP_ERR_TMA;
+}
+
 int check_common(int H, int B, int D, int E, int dtype) {
   if (H < 0 || B < 0 || D < 0 || E < 0) return FMLP_ERR_INVALID_SHAPE;
   if (dtype != FMLP_DTYPE_F16 && dtype != FMLP_DTYPE_BF16 && dtype != FMLP_DTYPE_F32)
@@ -214,6 +226,7 @@ const char* fmlp_error_string(int code) {
     case FMLP_ERR_PEER_ABORT:
       return "a rank of the fused all-reduce group gave up on a barrier (now or in an earlier call); "
              "every rank should stop";
+    case FMLP_ERR_INVALID_SCALE: return "fmlp_fwd_fp8: every scale must be finite and > 0";
   }
   return "unknown error";
 }
@@ -278,6 +291,42 @@ int fmlp_fwd(const void* x, const void* w1, const void* w2, void* o, int H, int 
 int fmlp_fwd_shared_x(const void* x, const void* w1, const void* w2, void* o, int H, int B, int D, int E,
                       int dtype, int act, void* stream) {
   return fwd_impl(x, w1, w2, o, H, B, D, E, dtype, act, 1, stream);
+}
+
+int fmlp_fwd_fp8(const void* x, const void* w1t, const void* w2t, void* o, int H, int B, int D, int E,
+                 float x_scale, float w1_scale, float w2_scale, float h_scale, int act, int out_dtype,
+                 void* stream) {
+  if (H < 0 || B < 0 || D < 0 || E < 0 || B > (1 << 30) || E > (1 << 30)) return FMLP_ERR_INVALID_SHAPE;
+  if ((long long)H * B * D >= (1LL << 40) || (long long)H * D * E >= (1LL << 40)) return FMLP_ERR_INVALID_SHAPE;
+  if (out_dtype != FMLP_DTYPE_BF16 && out_dtype != FMLP_DTYPE_F16) return FMLP_ERR_UNSUPPORTED_DTYPE;
+  if (D % 16 != 0 || D > 128) return FMLP_ERR_UNSUPPORTED_D;
+  if (E % 16 != 0) return FMLP_ERR_UNSUPPORTED_E;  // W2^T rows of E bytes: 16-byte strides
+  const float sc[4] = {x_scale, w1_scale, w2_scale, h_scale};
+  for (float v : sc)
+    if (!(v > 0.f) || !(v < 3.0e38f)) return FMLP_ERR_INVALID_SCALE;  // also rejects NaN
+  DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (size_t(H) * B * D == 0) return FMLP_OK;
+  if (E == 0) return cuda_rc(cudaMemsetAsync(o, 0, size_t(H) * B * D * 2, st));
+  if (!aligned16(x) || !aligned16(w1t) || !aligned16(w2t) || !aligned16(o)) return FMLP_ERR_MISALIGNED;
+  Fp8FwdLaunch a{};
+  // e4m3 tensors as bytes; boxes of 128 x 128 bytes, 128-byte swizzle (all K-major)
+  if ((rc = encode3d_u8(&a.tm_x, x, D, B, H))) return rc;
+  if ((rc = encode3d_u8(&a.tm_w1t, w1t, D, E, H))) return rc;
+  if ((rc = encode3d_u8(&a.tm_w2t, w2t, E, D, H))) return rc;
+  a.o = o;
+  a.H = H, a.B = B, a.D = D, a.E = E;
+  a.z_scale = x_scale * w1_scale;
+  a.h_inv_scale = 1.0f / h_scale;
+  a.o_scale = h_scale * w2_scale;
+  a.act = act;
+  a.out_bf16 = out_dtype == FMLP_DTYPE_BF16;
+  a.sm_count = dev->sm_count;
+  a.status = dev->status;
+  a.stream = st;
+  return cuda_rc(launch_fwd_fp8(a));
 }
 
 size_t fmlp_bwd_workspace_size_min(int H, int B, int D, int E, int dtype) {

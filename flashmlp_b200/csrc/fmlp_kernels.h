@@ -23,6 +23,25 @@ struct FwdLaunch {
   cudaStream_t stream;
 };
 
+// FP8 (e4m3) forward (fmlp_fwd_fp8.cu): per-tensor scales, the weights pre-transposed
+// so that every shared-memory operand is K-major.
+struct Fp8FwdLaunch {
+  CUtensorMap tm_x;    // X   (H,B,D) e4m3 viewed {D, B, H}, box {128, 128, 1}
+  CUtensorMap tm_w1t;  // W1^T (H,E,D) e4m3 viewed {D, E, H}, box {128, 128, 1}
+  CUtensorMap tm_w2t;  // W2^T (H,D,E) e4m3 viewed {E, D, H}, box {128, 128, 1}
+  void* o;             // O (H,B,D) in bf16 or fp16
+  int H, B, D, E;
+  float z_scale;       // x_scale * w1_scale: Z = (X8 @ W1_8) * z_scale
+  float h_inv_scale;   // 1 / h_scale: H8 = e4m3(act(Z) / h_scale), saturating
+  float o_scale;       // h_scale * w2_scale: O = (H8 @ W2_8) * o_scale
+  int act;
+  int out_bf16;        // 1 = bfloat16 output, 0 = float16
+  int sm_count;
+  uint32_t* status;
+  cudaStream_t stream;
+};
+cudaError_t launch_fwd_fp8(const Fp8FwdLaunch& a);
+
 // Tensor maps of the fp32 (TF32) backward: *_k with the 128-byte swizzle (tiles read
 // K-major), *_mn with the 128-byte swizzle of 32-byte atoms (tiles read MN-major, the
 // only MN-major layout of TF32 operands). Boxes {32 elements, rows}: X, dO and W2 32 rows,

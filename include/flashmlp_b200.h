@@ -51,6 +51,7 @@ extern "C" {
                                        FMLP_NOALLOC_SCRATCH_BYTES                      */
 #define FMLP_ERR_PEER_ABORT 12      /* fmlp_grad_allreduce_sgd: a rank of the group gave
                                        up on a barrier (now or in an earlier call)     */
+#define FMLP_ERR_INVALID_SCALE 13   /* fmlp_fwd_fp8: a scale is not finite and > 0      */
 
 /*
  * Forward. Replaces flashmlp_fwd + flashmlp_fwd_kernel (flashmlp.py:428-477, :63-158).
@@ -78,6 +79,21 @@ int fmlp_bwd(const void* x, const void* w1, const void* w2, const void* dO, void
  */
 int fmlp_fwd_shared_x(const void* x, const void* w1, const void* w2, void* o, int H, int B, int D,
                       int E, int dtype, int act, void* stream);
+
+/*
+ * FP8 (e4m3) forward with per-tensor scales. No counterpart in the reference, which has
+ * 16-bit and fp32 paths only; it is the forward of fmlp_fwd with 8-bit operands:
+ *   Z  = (x @ W1) * x_scale * w1_scale                 fp32 accumulation
+ *   H8 = e4m3(act(Z) / h_scale)                        round to nearest even, saturating
+ *   o  = (H8 @ W2) * h_scale * w2_scale                rounded to out_dtype (F16 / BF16)
+ * x (H,B,D) holds e4m3 bytes; the weights come TRANSPOSED, w1t (H,E,D) = W1^T and
+ * w2t (H,D,E) = W2^T, also e4m3 bytes (prepare them once per weight update); o (H,B,D)
+ * in out_dtype is fully written. Needs D % 16 == 0, D <= 128, E % 16 == 0, 16-byte
+ * aligned pointers and finite positive scales.
+ */
+int fmlp_fwd_fp8(const void* x, const void* w1t, const void* w2t, void* o, int H, int B, int D, int E,
+                 float x_scale, float w1_scale, float w2_scale, float h_scale, int act, int out_dtype,
+                 void* stream);
 
 /*
  * Backward of fmlp_fwd_shared_x: dO (B,D) is the gradient of the head mean, dx (B,D) the

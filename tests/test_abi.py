@@ -42,7 +42,7 @@ def test_python_constants_match_header():
 def test_error_strings_and_version():
     L = _lib.lib()
     assert L.fmlp_abi_version() == 100
-    for code in range(0, 13):
+    for code in range(0, 14):
         s = L.fmlp_error_string(code).decode()
         assert s and s != "unknown error"
     assert L.fmlp_error_string(99).decode() == "unknown error"
@@ -73,3 +73,21 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "libflashmlp_b200.so")
     with pytest.raises(ImportError, match="not built"):
         _lib.lib()
+
+
+def test_fp8_forward_validation_without_device():
+    """fmlp_fwd_fp8 rejects bad shapes, output dtypes and scales before any CUDA call."""
+    L = _lib.lib()
+    nul = ctypes.c_void_p(0)
+    d = header_defines()
+    ok_scales = (1.0, 1.0, 1.0, 1.0)
+    def call(H, B, D, E, scales=ok_scales, out=1):
+        return L.fmlp_fwd_fp8(nul, nul, nul, nul, H, B, D, E, *scales, 2, out, nul)
+    assert call(-1, 128, 64, 128) == d["FMLP_ERR_INVALID_SHAPE"]
+    assert call(1, 128, 64, 128, out=2) == d["FMLP_ERR_UNSUPPORTED_DTYPE"]  # fp32 output
+    assert call(1, 128, 144, 128) == d["FMLP_ERR_UNSUPPORTED_D"]             # D > 128
+    assert call(1, 128, 72, 128) == d["FMLP_ERR_UNSUPPORTED_D"]              # D % 16
+    assert call(1, 128, 64, 136) == d["FMLP_ERR_UNSUPPORTED_E"]              # E % 16
+    assert call(1, 128, 64, 128, (1.0, 0.0, 1.0, 1.0)) == d["FMLP_ERR_INVALID_SCALE"]
+    assert call(1, 128, 64, 128, (1.0, 1.0, float("nan"), 1.0)) == d["FMLP_ERR_INVALID_SCALE"]
+    assert call(1, 128, 64, 128, (1.0, 1.0, 1.0, float("inf"))) == d["FMLP_ERR_INVALID_SCALE"]
