@@ -555,6 +555,11 @@ def run_ours(args, rank, world, local_rank):
     rates = gather([cin, cout])
     del dev_out, pipe
 
+    # ---- FP8 (e4m3) forward of the same shard (not in the reference)
+    fp8 = None
+    if not args.no_fp8:
+        fp8 = run_fp8_leg(F, x, w1, w2, act, n, barrier, max_over_ranks, gather)
+
     # ---- C5 at the same N (batch-sharded training step)
     del x, w1, w2, do
     torch.cuda.empty_cache()
@@ -645,12 +650,55 @@ def run_ours(args, rank, world, local_rank):
                                            d2h / (min(r[1] for r in rates) * 1e9)) * 1e3, 3),
                 "numa": numa},
         "c5": c5,
+        "fp8_forward": None if fp8 is None else dict(
+            fp8, tflops=round(fwd_fl / (fp8["ms"] / 1e3) / 1e12, 2),
+            speedup_vs_bf16_forward=round(fwd_avg / fp8["ms"], 3)),
         "gpu_launches": launches_per_step * n,
         "clocks": clocks,
         "device_status": status,
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def run_fp8_leg(F, x, w1, w2, act, n, barrier, max_over_ranks, gather):
+    """The shard's forward in FP8 (flashmlp_fwd_fp8): X, W1, W2 quantized to e4m3 with
+    per-tensor scales, h_scale from the amax of head 0's activations, head 0 of the output
+    checked against the quantized fp32 reference (norm-wise), then `n` forwards timed on
+    the device (max over ranks)."""
+    import torch
+
+    acts = {"silu": torch.nn.functional.silu, "sigmoid": torch.sigmoid,
+            "leaky_relu": lambda z: torch.nn.functional.leaky_relu(z, 0.01)}
+    actf = acts.get(act, lambda z: z)
+    x8, sx = F.quantize_e4m3(x)
+    W = F.prepare_fp8_weights(w1, w2)
+    z0 = torch.mm(x8[0].float(), W.w1t[0].float().t()) * (sx * W.w1_scale)
+    h0 = actf(z0)
+    sh = max(float(h0.abs().max()) / 448.0, 1e-6)
+    h8 = (h0 / sh).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).float()
+    r0 = torch.mm(h8, W.w2t[0].float().t()) * (sh * W.w2_scale)
+    del z0, h0, h8
+    o = F.flashmlp_fwd_fp8(x8, W, act, x_scale=sx, h_scale=sh)
+    rel = float((o[0].float() - r0).norm() / r0.norm())
+    del o, r0
+    for _ in range(3):
+        F.flashmlp_fwd_fp8(x8, W, act, x_scale=sx, h_scale=sh)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        F.flashmlp_fwd_fp8(x8, W, act, x_scale=sx, h_scale=sh)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks([e0.elapsed_time(e1) / n])[0]
+    rels = gather([rel])
+    del x8, W
+    torch.cuda.empty_cache()
+    return {"ms": round(ms, 4), "max_norm_rel_err_head0": float(f"{max(r[0] for r in rels):.3e}"),
+            "kernel": "fmlp_fwd_fp8_kernel (tcgen05.mma kind::f8f6f4, e4m3 x e4m3, fp32 accumulation)",
+            "what": "flashmlp_fwd_fp8 of the same shard: per-tensor e4m3 scales, H8 = e4m3(act(Z) / h_scale), "
+                    "bf16 output; head 0 checked against the quantized fp32 reference"}
 
 
 def run_c5_leg(args, rank, world, dev, barrier, max_over_ranks, gather):
@@ -767,6 +815,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c5", action="store_true", help="skip the C5 batch-sharded leg")
+    ap.add_argument("--no-fp8", action="store_true", help="skip the FP8 forward leg")
     ap.add_argument("--no-triton", action="store_true", help="reference arm: skip the Triton-on-GPU timing")
     args = ap.parse_args()
     if args.warmup < 3:

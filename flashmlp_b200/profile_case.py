@@ -29,6 +29,8 @@ def main() -> None:
     ap.add_argument("--only", choices=["fwd", "bwd", "both"], default="both")
     ap.add_argument("--shared", action="store_true",
                     help="shared-input kernels: one (B, D) input for all heads, head mean output")
+    ap.add_argument("--fp8", action="store_true",
+                    help="instead: the FP8 forward (flashmlp_fwd_fp8) on the e4m3-quantized inputs")
     ap.add_argument("--allreduce", action="store_true",
                     help="instead: fmlp_grad_allreduce_sgd (one rank) and fmlp_sgd_update on 2*H*D*E weights")
     a = ap.parse_args()
@@ -41,6 +43,18 @@ def main() -> None:
     do = torch.randn(H, B, D, device="cuda", generator=g).to(dt)
     if a.allreduce:
         _allreduce(a, H, D, E, dt)
+        return
+    if a.fp8:
+        from . import fp8
+        x8, sx = fp8.quantize_e4m3(x)
+        wq = fp8.prepare_fp8_weights(w1, w2)
+        for _ in range(a.iters):
+            fp8.flashmlp_fwd_fp8(x8, wq, a.act, x_scale=sx, h_scale=0.01)
+        torch.cuda.synchronize()
+        st = _lib.lib().fmlp_device_status(1)
+        print(f"profile_case fp8 H={H} B={B} D={D} E={E} {a.act}: status {st}")
+        if st:
+            raise SystemExit(1)
         return
     if a.shared:
         x, do = x[0].contiguous(), do[0].contiguous()
