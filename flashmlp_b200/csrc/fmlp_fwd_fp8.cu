@@ -62,6 +62,39 @@ __device__ __forceinline__ uint32_t pack_e4m3x4(float a0, float a1, float a2, fl
   return lo | (hi << 16);
 }
 
+// act(z * z_scale) * h_inv_scale for the pair (v0, v1), two elements per instruction
+// (sm_100's packed fp32 forms). The SFU is this kernel's bound (75 % busy against 35 % for
+// the tensor pipe at 8 bits), so pairs with pair % FMLP_FP8_FMA_EVERY ==
+// FMLP_FP8_FMA_EVERY - 1 evaluate the sigmoid on the FMA pipe instead (sigmoid2_fma, max
+// relative error 8.1e-5, below tanh.approx's); measured at C4: every 8th pair 1.37 ->
+// 1.34 ms, every 6th the same, every 4th 1.49 ms (the FMA/ALU pipes fill), 0 = never.
+#ifndef FMLP_FP8_FMA_EVERY
+#define FMLP_FP8_FMA_EVERY 8
+#endif
+template <int ACT>
+__device__ __forceinline__ uint64_t act_fwd_scaled_pair(uint32_t v0, uint32_t v1, uint64_t zs2, uint64_t his2,
+                                                        int pair) {
+  const uint64_t z = mul2(f2(__uint_as_float(v0), __uint_as_float(v1)), zs2);
+  uint64_t h;
+  if constexpr (ACT == kSilu || ACT == kSigmoid) {
+    const uint64_t half = f2(0.5f, 0.5f);
+    if (FMLP_FP8_FMA_EVERY > 0 && pair % (FMLP_FP8_FMA_EVERY > 0 ? FMLP_FP8_FMA_EVERY : 1) == FMLP_FP8_FMA_EVERY - 1) {
+      const uint64_t sg = sigmoid2_fma(z);
+      h = ACT == kSilu ? mul2(z, sg) : sg;
+    } else {
+      const uint64_t u = mul2(half, z);
+      const uint64_t t = f2(tanh_approx(f2_lo(u)), tanh_approx(f2_hi(u)));
+      h = ACT == kSilu ? fma2(u, t, u) : fma2(half, t, half);  // u tanh(u) + u, or sigma
+    }
+  } else if constexpr (ACT == kLeakyRelu) {
+    const uint64_t m = mul2(f2(0.01f, 0.01f), z);
+    h = f2(fmaxf(f2_lo(z), f2_lo(m)), fmaxf(f2_hi(z), f2_hi(m)));
+  } else {
+    h = z;
+  }
+  return mul2(h, his2);
+}
+
 template <typename TO, int ACT>
 __global__ void __launch_bounds__(608, 1)
     fmlp_fwd_fp8_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w1t,
@@ -242,6 +275,7 @@ __global__ void __launch_bounds__(608, 1)
     const uint32_t lane_off = uint32_t(q * 32) << 16;
     uint32_t it = 0;
     bool ok = true;
+    const uint64_t zs2 = f2(z_scale, z_scale), his2 = f2(h_inv_scale, h_inv_scale);
     for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++it) {
       const int h = item / nP, pr = item % nP;
       for (int c = 0; c < nE && ok; ++c) {
@@ -254,11 +288,9 @@ __global__ void __launch_bounds__(608, 1)
           tmem_ld32_sync(za, v);
 #pragma unroll
           for (int i = 0; i < SW / 4; ++i) {
-            float hq[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              hq[u] = act_fwd<__nv_bfloat16, ACT>(__uint_as_float(v[4 * i + u]) * z_scale) * h_inv_scale;
-            p[i] = pack_e4m3x4(hq[0], hq[1], hq[2], hq[3]);
+            const uint64_t q0 = act_fwd_scaled_pair<ACT>(v[4 * i], v[4 * i + 1], zs2, his2, 2 * i);
+            const uint64_t q1 = act_fwd_scaled_pair<ACT>(v[4 * i + 2], v[4 * i + 3], zs2, his2, 2 * i + 1);
+            p[i] = pack_e4m3x4(f2_lo(q0), f2_hi(q0), f2_lo(q1), f2_hi(q1));
           }
           tmem_st8(za, p);  // H8 over the first 8 columns of the slice, just read
           tmem_wait_st();

@@ -626,6 +626,44 @@ __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {  // a - b
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Logistic sigmoid of a pair on the FMA/ALU pipes only (no SFU op), for activation warps
+// whose MUFU unit is the bottleneck: sigma(z) = 1 / (1 + 2^x), x = -z log2(e).
+//  * 2^x: x clamped to [-126, 126], split as x = n + f with n = round(x) by the
+//    1.5 * 2^23 addition (n lands in the low mantissa bits of t), f in [-0.5, 0.5];
+//    2^f by a degree-3 polynomial whose coefficients minimise the maximum relative error
+//    on that interval (Remez exchange, max relative error 7.5e-5), and 2^n added to its
+//    exponent field (bits(p) + (bits(t) << 23): the high bits of t's exponent shift out).
+//  * 1 / d, d = 1 + 2^x in [1, 2^126]: first estimate from the bit pattern,
+//    bits(r0) = 0x7EF311C2 - bits(d) (constant chosen to minimise the maximum relative
+//    error of r0 over a binade, 5.1 %), then two Newton steps r <- r (2 - d r).
+// Overall max relative error of sigma 8.1e-5 for z > -80 (tanh.approx-based: about 5e-4);
+// below -87 the clamp keeps sigma at about 2^-126 instead of smaller.
+__device__ __forceinline__ uint64_t sigmoid2_fma(uint64_t z) {
+  const uint64_t x0 = mul2(z, f2(-1.4426950408889634f, -1.4426950408889634f));
+  const uint64_t x = f2(fminf(fmaxf(f2_lo(x0), -126.f), 126.f), fminf(fmaxf(f2_hi(x0), -126.f), 126.f));
+  const uint64_t magic = f2(12582912.f, 12582912.f);
+  const uint64_t t = add2(x, magic);
+  const uint64_t f = sub2(x, sub2(t, magic));
+  uint64_t p = fma2(f2(0.0551716685295105f, 0.0551716685295105f), f, f2(0.2426111251115799f, 0.2426111251115799f));
+  p = fma2(p, f, f2(0.6932609677314758f, 0.6932609677314758f));
+  p = fma2(p, f, f2(0.9999280571937561f, 0.9999280571937561f));
+  const uint32_t e0 = __float_as_uint(f2_lo(p)) + (__float_as_uint(f2_lo(t)) << 23);
+  const uint32_t e1 = __float_as_uint(f2_hi(p)) + (__float_as_uint(f2_hi(t)) << 23);
+  const uint64_t d = add2(f2(__uint_as_float(e0), __uint_as_float(e1)), f2(1.f, 1.f));
+  const uint64_t nd = sub2(f2(0.f, 0.f), d);
+  uint64_t r = f2(__uint_as_float(0x7EF311C2u - __float_as_uint(f2_lo(d))),
+                  __uint_as_float(0x7EF311C2u - __float_as_uint(f2_hi(d))));
+  const uint64_t two = f2(2.f, 2.f);
+  r = mul2(r, fma2(nd, r, two));
+  r = mul2(r, fma2(nd, r, two));
+  return r;
+}
 
 // Activation codes shared with the host (see include/flashmlp_b200.h).
 enum Act : int { kLinear = 0, kLeakyRelu = 1, kSilu = 2, kSigmoid = 3 };
