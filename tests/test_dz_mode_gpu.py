@@ -133,6 +133,28 @@ def test_dz_mode_split_dw_c4_per_gpu_at_8():
     assert torch.equal(dwf[n1:].view(H, E, D).to(dt), got[2])
 
 
+def test_dz_mode_split_dw_d256():
+    # 128 < D <= 256: two dW programs per (head, E chunk), one per D half; with few heads the
+    # launch splits them over B ranges too (fp32 partials, ordered reduce).
+    H, B, D, E = 2, 16384, 256, 1024
+    dt = torch.float16
+    mode, splits, launches = _plan(H, B, D, E, dt)
+    assert mode == 1 and splits > 1 and launches == 3
+    x, w1, w2, do = make_inputs(H, B, D, E, dt, seed=21)
+    got = F().flashmlp_bwd(x, w1, w2, do, "sigmoid")
+    refs = ref_bwd(x, w1, w2, do, "sigmoid")
+    for i, k in enumerate(("dx", "dw1", "dw2")):
+        assert_close(got[i], *refs[k], dt, "bwd", f"d256 split {k}")
+    with F().low_memory_backward():  # recompute mode: one dW program per (head, chunk, half)
+        slow = F().flashmlp_bwd(x, w1, w2, do, "sigmoid")
+    assert torch.equal(got[0], slow[0])  # dX: the same dZ, the same GEMM order
+    dxf, dwf = F().flashmlp_bwd_dw_f32(x, w1, w2, do, "sigmoid")
+    n1 = H * D * E
+    assert torch.equal(dxf, got[0])
+    assert torch.equal(dwf[:n1].view(H, D, E).to(dt), got[1])
+    assert torch.equal(dwf[n1:].view(H, E, D).to(dt), got[2])
+
+
 def test_dz_mode_shared_input():
     # 2-D input: dZ^T of every head already carries the head mean's 1/H; the dX GEMM sums
     # over (head, e). Checked against the backward of the explicitly expanded input.
