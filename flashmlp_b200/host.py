@@ -61,10 +61,15 @@ class HostPipeline:
         hg = min(self.hg, max(H, 1))
         bufs = self._buffers(((hg, B, D), (hg, D, E), (hg, E, D)), x.dtype)
         groups = [(h0, min(h0 + hg, H)) for h0 in range(0, H, hg)]
-        ev_in = [torch.cuda.Event() for _ in groups]
+        # Per group, the forward needs only X, W1, W2 and its output O can go back while the
+        # backward runs, so the copies are split: X, W1, W2 in -> forward -> (O out | dO in)
+        # -> backward -> dX, dW1, dW2 out. The pipeline's fill (before the first kernel) and
+        # drain (after the last) then carry about half the bytes of a group each way.
+        ev_xw = [torch.cuda.Event() for _ in groups]
+        ev_do = [torch.cuda.Event() for _ in groups]
+        ev_fwd = [torch.cuda.Event() for _ in groups]
         ev_comp = [torch.cuda.Event() for _ in groups]
         ev_out = [torch.cuda.Event() for _ in groups]
-        results = [None] * len(groups)
         # the slots may still be read by the previous call's work, and the caller's stream
         # may have queued work this call must follow
         self.s_in.wait_stream(self.s_out)
@@ -75,23 +80,31 @@ class HostPipeline:
             if g >= self.slots:  # the slot's previous group has been copied out
                 self.s_in.wait_event(ev_out[g - self.slots])
             with torch.cuda.stream(self.s_in):
-                for k, src in (("x", x), ("w1", w1), ("w2", w2), ("do", do)):
+                for k, src in (("x", x), ("w1", w1), ("w2", w2)):
                     slot[k][:n].copy_(src[a:b], non_blocking=True)
-                ev_in[g].record(self.s_in)
-            self.s_comp.wait_event(ev_in[g])
+                ev_xw[g].record(self.s_in)
+                slot["do"][:n].copy_(do[a:b], non_blocking=True)
+                ev_do[g].record(self.s_in)
+            xs, w1s, w2s, dos = (slot[k][:n] for k in ("x", "w1", "w2", "do"))
+            self.s_comp.wait_event(ev_xw[g])
             with torch.cuda.stream(self.s_comp):
-                xs, w1s, w2s, dos = (slot[k][:n] for k in ("x", "w1", "w2", "do"))
                 o = flashmlp_fwd(xs, w1s, w2s, activation)
-                dx, dw1, dw2 = flashmlp_bwd(xs, w1s, w2s, dos, activation)
-                results[g] = (o, dx, dw1, dw2)
+                ev_fwd[g].record(self.s_comp)
+            self.s_out.wait_event(ev_fwd[g])
+            with torch.cuda.stream(self.s_out):
+                o_h[a:b].copy_(o, non_blocking=True)
+                o.record_stream(self.s_out)
+            self.s_comp.wait_event(ev_do[g])
+            with torch.cuda.stream(self.s_comp):
+                grads = flashmlp_bwd(xs, w1s, w2s, dos, activation)
                 ev_comp[g].record(self.s_comp)
             self.s_out.wait_event(ev_comp[g])
             with torch.cuda.stream(self.s_out):
-                for dst, src in zip((o_h, dx_h, dw1_h, dw2_h), results[g]):
+                for dst, src in zip((dx_h, dw1_h, dw2_h), grads):
                     dst[a:b].copy_(src, non_blocking=True)
                     src.record_stream(self.s_out)
                 ev_out[g].record(self.s_out)
-            results[g] = None
+            del o, grads
         torch.cuda.current_stream(self.device).wait_stream(self.s_out)
         return o_h, dx_h, dw1_h, dw2_h
 
