@@ -27,13 +27,14 @@ class HostPipeline:
     `heads_per_group` heads move and compute together; `slots` groups are in flight
     (3: one being copied in, one computing, one being copied out)."""
 
-    def __init__(self, device=None, heads_per_group: int = 4, slots: int = 3):
+    def __init__(self, device=None, heads_per_group: int = 4, slots: int = 3, ramp: bool = True):
         dev = torch.device(device) if device is not None else torch.device("cuda")
         if dev.type != "cuda":
             raise RuntimeError("fwd_bwd_host computes on a CUDA device")
         self.device = dev if dev.index is not None else torch.device("cuda", torch.cuda.current_device())
         self.hg = max(1, int(heads_per_group))
         self.slots = max(2, int(slots))
+        self.ramp = bool(ramp)
         self.s_in = torch.cuda.Stream(self.device)
         self.s_comp = torch.cuda.Stream(self.device)
         self.s_out = torch.cuda.Stream(self.device)
@@ -49,6 +50,23 @@ class HostPipeline:
             self._key = key
         return self._buf
 
+    def _groups(self, H: int, hg: int):
+        """Head ranges of the pipeline. With `ramp` (and room for it) the first and last
+        groups are smaller (hg/4, hg/2, ..., hg/2, hg/4 heads), so that the copy-in before
+        the first kernel and the copy-out after the last one are short."""
+        if self.ramp and hg >= 2 and H >= 3 * hg:
+            ends = sorted({max(1, hg // 4), max(1, hg // 2)})
+            mid = H - 2 * sum(ends)
+            sizes = ends + [hg] * (mid // hg) + ([mid % hg] if mid % hg else []) + ends[::-1]
+        else:
+            sizes = [min(hg, H - h0) for h0 in range(0, H, hg)]
+        out, h0 = [], 0
+        for n in sizes:
+            out.append((h0, h0 + n))
+            h0 += n
+        assert h0 == H
+        return out
+
     def run(self, x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, do: torch.Tensor, activation: str = "",
             out: Optional[Tuple[torch.Tensor, ...]] = None):
         """x, do (H, B, D), w1 (H, D, E), w2 (H, E, D) in (preferably pinned) host memory.
@@ -60,7 +78,7 @@ class HostPipeline:
         o_h, dx_h, dw1_h, dw2_h = out
         hg = min(self.hg, max(H, 1))
         bufs = self._buffers(((hg, B, D), (hg, D, E), (hg, E, D)), x.dtype)
-        groups = [(h0, min(h0 + hg, H)) for h0 in range(0, H, hg)]
+        groups = self._groups(H, hg)
         # Per group, the forward needs only X, W1, W2 and its output O can go back while the
         # backward runs, so the copies are split: X, W1, W2 in -> forward -> (O out | dO in)
         # -> backward -> dX, dW1, dW2 out. The pipeline's fill (before the first kernel) and
