@@ -217,6 +217,46 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- reference arm
+# The four configurations the reference publishes timings for (performance.md; bf16, silu,
+# FlashMLP module on a 3-D input), timed the way its example.py does: wall clock over 100
+# calls after 10 warm-ups, module and autograd overhead included.
+PUBLISHED_CONFIGS = [(8, 512, 64, 512), (12, 1024, 64, 768), (16, 2048, 64, 1024), (32, 4096, 64, 512)]
+
+
+def time_published_configs(module_cls, warmup=10, iters=100):
+    """fwd and fwd+bwd (o.sum().backward()) wall-clock ms of `module_cls(H, D, E, ...)` at
+    the reference's published configurations on cuda:0."""
+    import numpy as np
+    import torch
+
+    out = []
+    for H, B, D, E in PUBLISHED_CONFIGS:
+        torch.manual_seed(0)
+        model = module_cls(H, D, E, activation="silu", dtype=torch.bfloat16, device="cuda")
+        x = torch.randn(H, B, D, device="cuda", dtype=torch.bfloat16) / np.sqrt(D)
+
+        def fwd():
+            return model(x)
+
+        def fwd_bwd():
+            x_in = x.detach().requires_grad_(True)
+            model(x_in).sum().backward()
+
+        res = {"config": [H, B, D, E]}
+        for name, fn in (("fwd_ms", fwd), ("fwd_bwd_ms", fwd_bwd)):
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(iters):
+                fn()
+            torch.cuda.synchronize()
+            res[name] = round((time.perf_counter() - t0) / iters * 1e3, 4)
+        out.append(res)
+        del model, x
+    return out
+
+
 def time_reference_triton(steps, warmup):
     """The reference's Triton wrappers (flashmlp.py:428-538, autotuned on first call) on
     cuda:0 at the full C4 shape, CUDA events on torch's current stream (the stream Triton
@@ -303,6 +343,10 @@ def run_reference(args, rank, world):
     if world == 1 and not args.no_triton:
         try:
             line["triton_b200"] = time_reference_triton(args.steps, args.warmup)
+            from oracle.reference_loader import load_reference
+            ref = load_reference()
+            if ref is not None:
+                line["triton_b200"]["published_configs"] = time_published_configs(ref.FlashMLP)
         except Exception as e:  # reported, not fatal: the line's value is the CPU path
             line["triton_b200"] = {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
     print(json.dumps(line), flush=True)
@@ -567,6 +611,8 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_c5:
         c5 = run_c5_leg(args, rank, world, dev, barrier, max_over_ranks, gather)
 
+    # the reference's published configurations, timed as its example.py does (N = 1 only)
+    pub = time_published_configs(F.FlashMLP) if (rank == 0 and world == 1) else None
     cpu = measure_cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if world > 1:
         dist.barrier()
@@ -650,6 +696,7 @@ def run_ours(args, rank, world, local_rank):
                                            d2h / (min(r[1] for r in rates) * 1e9)) * 1e3, 3),
                 "numa": numa},
         "c5": c5,
+        "published_configs": pub,
         "fp8_forward": None if fp8 is None else dict(
             fp8, tflops=round(fwd_fl / (fp8["ms"] / 1e3) / 1e12, 2),
             speedup_vs_bf16_forward=round(fwd_avg / fp8["ms"], 3)),

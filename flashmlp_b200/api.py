@@ -62,6 +62,19 @@ def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
     return ctypes.c_void_p(t.data_ptr())
 
 
+def _on_device(dev: torch.device):
+    """torch.cuda.device(dev), or nothing when dev is already the current device (the
+    common case; the context manager costs microseconds per call at small shapes)."""
+    if dev.index is None or dev.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(dev)
+
+
+# fmlp_bwd_workspace_size per (device, shape, dtype): it depends only on those (the SM
+# count enters the split rule), and the lookup is on the per-call host path
+_WS_FULL = {}
+
+
 _WS_LIMIT = threading.local()
 
 
@@ -94,7 +107,10 @@ def low_memory_backward(enabled: bool = True):
 
 
 def _bwd_workspace_bytes(L, H: int, B: int, D: int, E: int, dt: int) -> int:
-    full = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
+    key = (torch.cuda.current_device(), H, B, D, E, dt)
+    full = _WS_FULL.get(key)
+    if full is None:
+        full = _WS_FULL[key] = int(L.fmlp_bwd_workspace_size(H, B, D, E, dt))
     lim = getattr(_WS_LIMIT, "v", None)
     if lim is None or lim >= full:
         return full
@@ -131,10 +147,10 @@ def flashmlp_fwd(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     dev = _check_tensors(x, w1, w2)
     o = torch.empty_like(x)
     L = _lib.lib()
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
-        rc = L.fmlp_fwd(_ptr(x), _ptr(w1), _ptr(w2), _ptr(o), H, B, D, E,
-                        _dtype_code(x), activation_code(activation), ctypes.c_void_p(stream))
+        rc = L.fmlp_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), o.data_ptr(), H, B, D, E,
+                        _dtype_code(x), activation_code(activation), stream)
     _lib.check(rc, "fmlp_fwd")
     return o.reshape(H, B, D)
 
@@ -170,15 +186,15 @@ def flashmlp_bwd(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     dw2 = torch.empty_like(w2)
     L = _lib.lib()
     dt = _dtype_code(x)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         # scratch: the dZ^T tiles of the dZ-store mode and/or the fp32 dW partial sums of
         # split dW programs
         ws_bytes = _bwd_workspace_bytes(L, H, B, D, E, dt)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
         stream = torch.cuda.current_stream(dev).cuda_stream
-        rc = L.fmlp_bwd(_ptr(x), _ptr(w1), _ptr(w2), _ptr(do), _ptr(dx), _ptr(dw1), _ptr(dw2),
-                        _ptr(ws) if ws is not None else None, ws_bytes, H, B, D, E, dt,
-                        activation_code(activation), ctypes.c_void_p(stream))
+        rc = L.fmlp_bwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), do.data_ptr(), dx.data_ptr(),
+                        dw1.data_ptr(), dw2.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes,
+                        H, B, D, E, dt, activation_code(activation), stream)
     _lib.check(rc, "fmlp_bwd")
     return dx.reshape(H, B, D), dw1.reshape(H, D, E), dw2.reshape(H, E, D)
 
