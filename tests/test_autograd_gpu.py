@@ -125,19 +125,20 @@ def test_drop_in_module_name():
     assert callable(flashmlp.flashmlp_fwd) and callable(flashmlp.flashmlp_bwd)
 
 
-def test_host_pipeline_matches_device_calls():
+@pytest.mark.parametrize("H,hg", [(7, 3), (13, 4)])  # (13, 4): groups ramp 1, 2, 4, 3, 2, 1
+def test_host_pipeline_matches_device_calls(H, hg):
     # host-resident inputs, head groups pipelined over three streams: same bits as the
     # device calls on the whole tensors (heads are independent); H not a multiple of the group
     import flashmlp_b200 as F
     from flashmlp_b200.host import HostPipeline
 
-    H, B, D, E = 7, 1000, 64, 264
+    B, D, E = 1000, 64, 264
     g = torch.Generator().manual_seed(3)
     x = torch.randn(H, B, D, generator=g).to(torch.bfloat16).pin_memory()
     w1 = (torch.randn(H, D, E, generator=g) / D ** 0.5).to(torch.bfloat16).pin_memory()
     w2 = (torch.randn(H, E, D, generator=g) / E ** 0.5).to(torch.bfloat16).pin_memory()
     do = torch.randn(H, B, D, generator=g).to(torch.bfloat16).pin_memory()
-    pipe = HostPipeline("cuda", heads_per_group=3)
+    pipe = HostPipeline("cuda", heads_per_group=hg)
     for _ in range(2):  # buffers reused on the second call
         outs = pipe.run(x, w1, w2, do, "silu")
         torch.cuda.synchronize()
