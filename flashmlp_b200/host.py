@@ -5,8 +5,11 @@ sits in host memory first copies X, W1, W2 and dO to the GPU and the results bac
 those copies (2 x 16-bit x (2*H*B*D + 2*H*D*E) bytes per step) take longer than the
 kernels over PCIe. Heads are independent, so `fwd_bwd_host` cuts the heads into groups
 and pipelines them over three CUDA streams: group g+1 is copied in while group g runs
-through flashmlp_fwd / flashmlp_bwd and group g-1 is copied out. Results are identical to
-flashmlp_fwd / flashmlp_bwd on the whole tensors (the kernels treat heads independently).
+through flashmlp_fwd / flashmlp_bwd and group g-1 is copied out. Results are those of
+flashmlp_fwd / flashmlp_bwd on each head group: O and dX are bit-identical to one call on
+the whole tensors (the kernels treat heads independently); dW can differ from it in the
+last bits, because a launch splits its dW sums over B ranges according to its head count
+and the fp32 partials are then added in a different grouping.
 """
 from __future__ import annotations
 

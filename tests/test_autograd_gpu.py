@@ -127,8 +127,8 @@ def test_drop_in_module_name():
 
 @pytest.mark.parametrize("H,hg", [(7, 3), (13, 4)])  # (13, 4): groups ramp 1, 2, 4, 3, 2, 1
 def test_host_pipeline_matches_device_calls(H, hg):
-    # host-resident inputs, head groups pipelined over three streams: same bits as the
-    # device calls on the whole tensors (heads are independent); H not a multiple of the group
+    # host-resident inputs, head groups pipelined over three streams: the same bits as the
+    # device calls on each head group; H not a multiple of the group
     import flashmlp_b200 as F
     from flashmlp_b200.host import HostPipeline
 
@@ -139,10 +139,21 @@ def test_host_pipeline_matches_device_calls(H, hg):
     w2 = (torch.randn(H, E, D, generator=g) / E ** 0.5).to(torch.bfloat16).pin_memory()
     do = torch.randn(H, B, D, generator=g).to(torch.bfloat16).pin_memory()
     pipe = HostPipeline("cuda", heads_per_group=hg)
+    xd, w1d, w2d, dod = x.cuda(), w1.cuda(), w2.cuda(), do.cuda()
+    whole = [F.flashmlp_fwd(xd, w1d, w2d, "silu"), *F.flashmlp_bwd(xd, w1d, w2d, dod, "silu")]
+    # per head group, as the pipeline launches them: dW too is bit-identical (a launch's
+    # dW split over B ranges depends on its head count, so against the whole-tensor call
+    # only O and dX are)
+    grouped = [[], [], [], []]
+    for a, b in pipe._groups(H, hg):
+        for k, t in enumerate([F.flashmlp_fwd(xd[a:b], w1d[a:b], w2d[a:b], "silu"),
+                               *F.flashmlp_bwd(xd[a:b], w1d[a:b], w2d[a:b], dod[a:b], "silu")]):
+            grouped[k].append(t)
+    grouped = [torch.cat(ts) for ts in grouped]
     for _ in range(2):  # buffers reused on the second call
         outs = pipe.run(x, w1, w2, do, "silu")
         torch.cuda.synchronize()
-        ref = [F.flashmlp_fwd(x.cuda(), w1.cuda(), w2.cuda(), "silu"),
-               *F.flashmlp_bwd(x.cuda(), w1.cuda(), w2.cuda(), do.cuda(), "silu")]
-        for a, r in zip(outs, ref):
+        for a, r in zip(outs, grouped):
             assert a.device.type == "cpu" and torch.equal(a, r.cpu())
+        for a, r in zip(outs[:2], whole[:2]):
+            assert torch.equal(a, r.cpu())
