@@ -1,9 +1,11 @@
 """FP8 (e4m3) forward (fmlp_fwd_fp8) against an fp32 PyTorch reference of the same
 quantized computation: Z from the dequantized e4m3 operands (their products are exact in
 fp32), act(Z) / h_scale rounded to e4m3 by torch's cast (saturated at 448 first), O from
-that and W2. The kernel's sigmoid/silu use the SFU tanh (relative error about 5e-4), which
-moves a small fraction of the e4m3 roundings of H by one step; the bounds below cover that
-and the bf16/fp16 output rounding. The reference has no FP8 path, so there is no golden.
+that and W2. The kernel's sigmoid/silu use the SFU tanh (relative error about 5e-4) on
+seven of every eight column pairs and a polynomial exp2 with a Newton reciprocal on the
+FMA pipe (relative error about 1e-4) on the eighth; either moves a small fraction of the
+e4m3 roundings of H by one step. The bounds below cover that and the bf16/fp16 output
+rounding. The reference has no FP8 path, so there is no golden.
 """
 import pytest
 import torch
