@@ -18,7 +18,7 @@ BUILD_DIR = PKG_DIR.parent / "_build"
 LIB_NAME = "libflashmlp_b200.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 SOURCES = ["fmlp_fwd.cu", "fmlp_fwd_pair.cu", "fmlp_fwd2sm.cu", "fmlp_fwd_fp8.cu", "fmlp_bwd.cu", "fmlp_bwd256.cu", "fmlp_capi.cu",
-           "fmlp_noalloc.cu", "fmlp_comm.cu", "fmlp_tf32.cu", "fmlp_dxgemm.cu"]
+           "fmlp_noalloc.cu", "fmlp_comm.cu", "fmlp_tf32.cu", "fmlp_dxgemm.cu", "fmlp_dwgemm256.cu"]
 HEADERS = ["fmlp_ptx.cuh", "fmlp_act.cuh", "fmlp_kernels.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -838,8 +838,9 @@ size_t bwd_workspace_bytes(int H, int B, int D, int E, int sm_count) {
 
 size_t bwd_dz_bytes(int H, int B, int D, int E, int sm_count, int elem_bytes) {
   if (D > (elem_bytes == 4 ? 128 : 256) || H <= 0 || B <= 0 || E <= 0 || sm_count <= 0) return 0;
-  const size_t nB = (size_t(B) + kRows - 1) / kRows, nE = (size_t(E) + kBwdEt - 1) / kBwdEt;
-  const size_t bytes = size_t(H) * nE * kBwdEt * nB * kRows * elem_bytes;
+  // dZ^T tiles; for 128 < D <= 256 (16-bit) the H^T tiles of the D-half-1 GEMM follow
+  const size_t regions = (D > 128 && elem_bytes == 2) ? 2 : 1;
+  const size_t bytes = dz_tile_elems(H, B, E) * elem_bytes * regions;
   return bytes <= kDzCapBytes ? bytes : 0;
 }
 
@@ -849,19 +850,20 @@ int bwd_dz_splits(int H, int B, int D, int E, int sm_count) {
   // The launch holds dW programs only, all of the same length, so it runs in whole waves
   // of sm_count programs: pick S (1..16, at least 2 B tiles per split) minimising
   // waves * (tiles per program + 2 for a program's fill and drain) * tile time + the fp32
-  // reduce of the partials (S > 1). For 128 < D <= 256 (fmlp_bwd256.cu) there are two
-  // programs per (head, E chunk), one per D half, each forming Z^T and dH^T over all of D.
+  // reduce of the partials (S > 1). For 128 < D <= 256 (fmlp_bwd256.cu) the launch holds
+  // the D-half-0 programs, each forming Z^T and dH^T over all of D, and the D-half-1 GEMM
+  // (fmlp_dwgemm256.cu) has as many programs, HBM-bound on the 64 KB of stored dZ^T and
+  // H^T tiles per 128-row tile.
   const int dp = D <= 64 ? 64 : (D <= 128 ? 128 : 256);
-  const int per_chunk = dp == 256 ? 2 : 1;
   const double tile_flop = dp == 256 ? 4.0 * 128 * 128 * 256 + 4.0 * 128 * 128 * 128  // Z^T, dH^T, two half dW
                                      : 8.0 * 128 * 128 * dp;                          // 4 products of 128x128xDP
-  const double tile_s = tile_flop / (1.2e15 / sm_count);
+  const double tile_s = tile_flop / (1.2e15 / sm_count) + (dp == 256 ? 65536.0 / (6.0e12 / sm_count) : 0.0);
   const double hde = double(H) * D * E;
   const long long max_s = nB / 2 < 16 ? nB / 2 : 16;
   int best = 1;
   double best_t = 0;
   for (long long s = 1; s <= (max_s < 1 ? 1 : max_s); ++s) {
-    const long long progs = (long long)H * nE * s * per_chunk;
+    const long long progs = (long long)H * nE * s;
     const long long waves = (progs + sm_count - 1) / sm_count;
     double t = double(waves) * double((nB + s - 1) / s + 2) * tile_s;
     if (s > 1) t += (8.0 * s + 4.0) * hde / 6.0e12 + 5e-6;

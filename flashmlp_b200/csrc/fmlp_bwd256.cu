@@ -33,8 +33,10 @@
 // Warp roles as in fmlp_bwd.cu: warp 0 TMA, warp 1 MMA, warps 2..17 activation (warp
 // (q, j) owns TMEM lanes [32q, 32q+32) and 16-column slice j of each 64-column product).
 //
-// dZ-store mode (as in fmlp_bwd.cu): the launch holds only the dW programs, those of D half
-// 0 also store their packed dZ^T tiles, and fmlp_dx_gemm_kernel (N = 256) forms dX.
+// dZ-store mode: the launch holds only the dW programs of D half 0, which also store their
+// packed dZ^T and H^T tiles; fmlp_dw_gemm256_kernel forms the D-half-1 dW from those tiles
+// (the same operands and order as a half-1 program, without its recompute of Z^T and dH^T)
+// and fmlp_dx_gemm_kernel (N = 256) forms dX.
 #include "fmlp_act.cuh"
 #include "fmlp_kernels.h"
 #include "fmlp_ptx.cuh"
@@ -86,7 +88,8 @@ __global__ void __launch_bounds__(576, 1)
                        const __grid_constant__ CUtensorMap tm_w2, const T* __restrict__ X,
                        const T* __restrict__ W1, T* __restrict__ dX, T* __restrict__ dW1,
                        T* __restrict__ dW2, float* __restrict__ dwf, float* __restrict__ part,
-                       T* __restrict__ dzt, int splits, int H, int B, int D, int E, uint32_t* status) {
+                       T* __restrict__ dzt, T* __restrict__ hts, int halves, int splits, int H, int B, int D,
+                       int E, uint32_t* status) {
   using C = Bwd256Cfg;
   using St = ActState<T, ACT>;
   constexpr int DP = C::DP;
@@ -105,15 +108,18 @@ __global__ void __launch_bounds__(576, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nEw = (E + C::EW - 1) / C::EW;  // dW programs per head, D half and B range
-  const int nW = H * nEw * 2 * splits;
+  // halves = 2: programs for both D halves; 1 (dZ-store mode): D half 0 only
+  const int nW = H * nEw * halves * splits;
   const bool is_dw = int(blockIdx.x) < nW;
   int h, idx, g = 0, split = 0;
   if (is_dw) {  // (head, B range, E chunk, D half), D half fastest
-    h = blockIdx.x / (nEw * 2 * splits);
-    const int r = blockIdx.x % (nEw * 2 * splits);
-    split = r / (nEw * 2);
-    idx = (r % (nEw * 2)) >> 1;  // E chunk
-    g = r & 1;                   // D half
+    const int per_h = nEw * halves * splits;
+    h = blockIdx.x / per_h;
+    const int r = blockIdx.x % per_h;
+    split = r / (nEw * halves);
+    const int rr = r % (nEw * halves);
+    idx = rr / halves;  // E chunk
+    g = rr % halves;    // D half
   } else {
     const int nBx = (B + BM - 1) / BM;
     const int p = blockIdx.x - nW;
@@ -169,10 +175,10 @@ __global__ void __launch_bounds__(576, 1)
   const int j = (warp - 2) >> 2;
   const uint32_t lane_off = uint32_t(q * 32) << 16;
 
-  // Phase 1 over the 16 product columns at `col`: derivative state; if `pack_h`, the packed
-  // H in the first 8 of those columns.
-  auto phase1 = [&](uint32_t col, St (&st)[16], bool pack_h) {
-    uint32_t v[16], p[8];
+  // Phase 1 over the 16 product columns at `col`: derivative state and the packed H in p;
+  // if `pack_h`, also written to the first 8 of those columns.
+  auto phase1 = [&](uint32_t col, St (&st)[16], bool pack_h, uint32_t (&p)[8]) {
+    uint32_t v[16];
     tmem_ld16_sync(col, v);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -353,13 +359,26 @@ __global__ void __launch_bounds__(576, 1)
       const uint32_t dz_off = uint32_t(((size_t(h) * nEw + c) * nB128 + bt0) * (BM * 128)) + (q >> 1) * 8192 +
                               (2 * j) * 512 + ((q & 1) * 32 + lane) * 8;
       T* const dz = (g == 0) ? dzt : nullptr;
+      // H^T tiles (dZ-store mode, for fmlp_dw_gemm256_kernel): one 128 x 128 tile per (head,
+      // E chunk, 128-row B tile) laid out [b / 8][e][b % 8], the K-major no-swizzle operand
+      // layout, so a 64-row half tile is 16 KB of contiguous memory; this thread writes the
+      // 8-b groups 8(t%2) + 2j and the next of row e.
+      const uint32_t h_off = uint32_t(((size_t(h) * nEw + c) * nB128 + bt0) * (BM * 128)) + (2 * j) * 1024 +
+                             (q * 32 + lane) * 8;
+      T* const hs = (g == 0) ? hts : nullptr;
       bool ok = true;
       for (int t = 0; t < nT && ok; ++t) {
         St st[16];
+        uint32_t ph[8];
         if (!(ok = mbar_wait(&p_full[0], t & 1, ctx))) break;
         tc_fence_after();
-        phase1(zt, st, true);  // H^T packed over Z^T
+        phase1(zt, st, true, ph);  // H^T packed over Z^T
         signal(&a_full[0], true);
+        if (hs != nullptr) {  // off the chain of the products waiting on a_full[0]
+          T* hp = hs + (h_off + uint32_t(t >> 1) * (BM * 128) + uint32_t(t & 1) * 8192);
+          *reinterpret_cast<uint4*>(hp) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+          *reinterpret_cast<uint4*>(hp + 1024) = make_uint4(ph[4], ph[5], ph[6], ph[7]);
+        }
         if (!(ok = mbar_wait(&p_full[1], t & 1, ctx))) break;
         tc_fence_after();
         phase2(dt, st, dz != nullptr ? dz + (dz_off + uint32_t(t >> 1) * (BM * 128) + uint32_t(t & 1) * 4096) : nullptr,
@@ -565,9 +584,10 @@ __global__ void __launch_bounds__(576, 1)
       bool ok = true;
       for (int c = 0; c < nE && ok; ++c) {
         St st[16];
+        uint32_t ph[8];
         if (!(ok = mbar_wait(&p_full[0], c & 1, ctx))) break;
         tc_fence_after();
-        phase1(za, st, false);  // derivative state only
+        phase1(za, st, false, ph);  // derivative state only
         signal(&a_full[0], false);
         if (!(ok = mbar_wait(&p_full[1], c & 1, ctx))) break;
         tc_fence_after();
@@ -606,19 +626,24 @@ static cudaError_t launch_bwd256_t(const BwdLaunch& a) {
   if (e != cudaSuccess) return e;
   const int nBx = (a.B + kRows - 1) / kRows;
   const int nEw = (a.E + C::EW - 1) / C::EW;
-  // dZ-store mode: dW programs only (they store dZ^T), then fmlp_dx_gemm_kernel forms dX
+  // dZ-store mode: the D-half-0 dW programs only (they store dZ^T and H^T), then
+  // fmlp_dw_gemm256_kernel forms the D-half-1 dW and fmlp_dx_gemm_kernel dX
   const bool dz = a.dzt != nullptr;
+  const int halves = dz ? 1 : 2;
+  T* const hts = dz ? reinterpret_cast<T*>(a.dzt) + dz_tile_elems(a.H, a.B, a.E) : nullptr;
   // dW programs over `splits` B ranges (fp32 partials reduced afterwards) when there are
   // too few (head, E chunk, D half) programs for the SMs
   const int splits = a.splits < 1 ? 1 : a.splits;
   if (splits > 1 && (a.part == nullptr || splits > nBx)) return cudaErrorInvalidValue;
-  const long long grid = (long long)a.H * (2LL * nEw * splits + (dz ? 0 : nBx));
+  const long long grid = (long long)a.H * ((long long)halves * nEw * splits + (dz ? 0 : nBx));
   if (grid <= 0 || grid > 0x7FFFFFFFLL) return cudaErrorInvalidValue;
   kern<<<unsigned(grid), C::NUM_THREADS, C::SMEM, a.stream>>>(
       a.tm_x, a.tm_do, a.tm_w1, a.tm_w2, reinterpret_cast<const T*>(a.x), reinterpret_cast<const T*>(a.w1),
       reinterpret_cast<T*>(a.dx), reinterpret_cast<T*>(a.dw1), reinterpret_cast<T*>(a.dw2), a.dw_f32,
-      splits > 1 ? a.part : nullptr, reinterpret_cast<T*>(a.dzt), splits, a.H, a.B, a.D, a.E, a.status);
+      splits > 1 ? a.part : nullptr, reinterpret_cast<T*>(a.dzt), hts, halves, splits, a.H, a.B, a.D, a.E,
+      a.status);
   cudaError_t le = cudaGetLastError();
+  if (le == cudaSuccess && dz) le = launch_dw_gemm256(a);
   if (le == cudaSuccess && dz) le = launch_dx_gemm(a);
   if (le != cudaSuccess || splits == 1) return le;
   return launch_dw_reduce(a);

@@ -364,7 +364,10 @@ int fmlp_bwd_plan(int H, int B, int D, int E, int dtype, size_t workspace_bytes,
   const int groups = p.dz ? (H + p.group - 1) / p.group : 1;
   if (mode) *mode = p.dz ? 1 : 0;
   if (splits) *splits = p.splits;
-  if (launches) *launches = empty ? 0 : groups * (1 + (p.dz ? 1 : 0) + (p.splits > 1 ? 1 : 0));
+  // dW programs, [D-half-1 dW GEMM (dZ-store mode, 128 < D <= 256)], [dX GEMM (dZ-store
+  // mode)], [ordered reduce of the split dW partials]
+  const int dw_gemm = (p.dz && !f32 && D > 128) ? 1 : 0;
+  if (launches) *launches = empty ? 0 : groups * (1 + dw_gemm + (p.dz ? 1 : 0) + (p.splits > 1 ? 1 : 0));
   return FMLP_OK;
 }
 

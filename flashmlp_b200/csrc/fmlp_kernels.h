@@ -81,6 +81,12 @@ constexpr int kRows = 128;  // rows of a B tile (tcgen05 M)
 inline int fwd_et(int dp) { return dp <= 128 ? 128 : 64; }
 constexpr int kBwdEt = 128;  // E chunk of both backward program kinds
 
+// Elements of one launch's stored dZ^T tiles (dZ-store mode): a 128 x 128 tile per (head,
+// 128-wide E chunk, 128-row B tile). For 128 < D <= 256 the H^T tiles follow, as many.
+inline size_t dz_tile_elems(int H, int B, int E) {
+  return size_t(H) * ((size_t(E) + kBwdEt - 1) / kBwdEt) * kBwdEt * ((size_t(B) + kRows - 1) / kRows) * kRows;
+}
+
 // Forward on CTA pairs (fmlp_fwd2sm.cu): 16-bit inputs, per-head X, DP in {128, 256};
 // a.tm_w2 must have boxes of 128 E rows.
 cudaError_t launch_fwd2sm(const FwdLaunch& a);
@@ -90,6 +96,8 @@ cudaError_t launch_fwd_pair(const FwdLaunch& a);  // two row tiles per CTA, D <=
 cudaError_t launch_bwd(const BwdLaunch& a);     // picks the kernel for a.dp
 cudaError_t launch_bwd256(const BwdLaunch& a);  // 128 < D <= 256
 cudaError_t launch_dx_gemm(const BwdLaunch& a);  // dX from the stored dZ^T (dZ-store mode)
+// D half 1 of dW for 128 < D <= 256 from the stored dZ^T and H^T tiles (dZ-store mode)
+cudaError_t launch_dw_gemm256(const BwdLaunch& a);
 // fixed-order sum of the a.splits fp32 dW partials at a.part into dw1/dw2 (or a.dw_f32)
 cudaError_t launch_dw_reduce(const BwdLaunch& a);
 cudaError_t launch_fwd_tf32(const FwdLaunch& a);  // fp32 inputs, TF32 products, D <= 128
@@ -110,7 +118,9 @@ int bwd_dz_splits_tf32(int H, int B, int D, int E, int sm_count);  // dZ-store m
 
 // dZ-store mode of the backward (16-bit inputs with D <= 256, fp32 inputs with D <= 128):
 // the dW programs also store dZ and a GEMM over E forms dX from it (fmlp_dxgemm.cu; fp32:
-// fmlp_tf32.cu). bwd_dz_bytes is the dZ workspace of one launch over H heads for elements
+// fmlp_tf32.cu); for 128 < D <= 256 they store H^T as well, and a GEMM over B forms the
+// second D half of dW from the two (fmlp_dwgemm256.cu). bwd_dz_bytes is the dZ (and H^T)
+// workspace of one launch over H heads for elements
 // of elem_bytes (0 when the mode does not apply or would need more than kDzCapBytes: the
 // kernels address a launch's dZ tiles with 32-bit element offsets); bwd_dz_splits the dW
 // split factor of that launch, whose fp32 partials follow the dZ region

@@ -123,8 +123,9 @@ int fmlp_bwd_dw_f32(const void* x, const void* w1, const void* w2, const void* d
  * D <= 256 and fp32 inputs with D <= 128 that is the dZ-store mode: the dW programs also
  * store their dZ (H * ceil(E/128)*128 * ceil(B/128)*128 values of the input dtype, at
  * most 8 GiB) and dX becomes a GEMM over E of those values instead of programs that
- * recompute Z and dH; plus the fp32 dW partial sums below when that launch splits its dW
- * programs.
+ * recompute Z and dH; for 128 < D <= 256 they also store H = act(Z) (as many values),
+ * from which with dZ a GEMM over B forms the second half of dW's D columns; plus the fp32
+ * dW partial sums below when that launch splits its dW programs.
  *
  * fmlp_bwd_workspace_size_min: the least workspace fmlp_bwd accepts (the recompute mode).
  * Nonzero only when the launch has too few (head, E chunk) pairs to fill the GPU (e.g. 4

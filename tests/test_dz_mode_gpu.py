@@ -11,7 +11,9 @@ bar as the recompute mode:
   tiles, D below the padded 64/128), every activation, bf16 and fp16, and against a
   plain PyTorch fp32 reference with magnitude bounds on longer batches;
 * against the recompute mode (the low-memory path) on the same inputs: dX within the
-  parity tolerance, dW bit-identical when both modes split the dW programs alike;
+  parity tolerance, dW bit-identical when both modes split the dW programs alike (for
+  128 < D <= 256 that covers the D-half-1 GEMM over the stored dZ^T and H^T tiles, which
+  must give the bits of the recompute mode's D-half-1 programs);
 * with split dW programs (few heads, many B tiles) and with a shared (2-D) input;
 * at the C4 per-GPU size of 8-way head sharding against a plain PyTorch fp32 reference;
 * the workspace region past the dZ^T tiles and the outputs' neighbours are not written;
@@ -92,7 +94,8 @@ def test_dz_mode_vs_torch_fp32_longer_batches(shape, dtype):
 
 
 @pytest.mark.parametrize("shape,dtype", [((8, 8192, 128, 1024), torch.bfloat16), ((6, 3000, 64, 520), torch.float16),
-                                         ((3, 4096, 256, 512), torch.float16)])
+                                         ((3, 4096, 256, 512), torch.float16), ((6, 256, 256, 1024), torch.bfloat16),
+                                         ((2, 200, 192, 264), torch.float16)])
 def test_dz_mode_matches_recompute_mode(shape, dtype):
     H, B, D, E = shape
     fast, slow = _plan(H, B, D, E, dtype), _plan(H, B, D, E, dtype, low_memory=True)
@@ -134,12 +137,13 @@ def test_dz_mode_split_dw_c4_per_gpu_at_8():
 
 
 def test_dz_mode_split_dw_d256():
-    # 128 < D <= 256: two dW programs per (head, E chunk), one per D half; with few heads the
-    # launch splits them over B ranges too (fp32 partials, ordered reduce).
+    # 128 < D <= 256: the dW programs of D half 0 store dZ^T and H^T, a GEMM over B forms D
+    # half 1 from them; with few heads both split over B ranges (fp32 partials, ordered
+    # reduce): dW programs, D-half-1 GEMM, dX GEMM, reduce.
     H, B, D, E = 2, 16384, 256, 1024
     dt = torch.float16
     mode, splits, launches = _plan(H, B, D, E, dt)
-    assert mode == 1 and splits > 1 and launches == 3
+    assert mode == 1 and splits > 1 and launches == 4
     x, w1, w2, do = make_inputs(H, B, D, E, dt, seed=21)
     got = F().flashmlp_bwd(x, w1, w2, do, "sigmoid")
     refs = ref_bwd(x, w1, w2, do, "sigmoid")
