@@ -238,16 +238,17 @@ def test_dz_mode_runs_in_head_groups_above_8_gib():
         _lib.bwd_plan(4, B, D, E, 1, need - 16)
 
 
-@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
-def test_dz_mode_head_groups_match_one_launch(dt):
+@pytest.mark.parametrize("dt,D", [(torch.bfloat16, 128), (torch.float32, 128), (torch.float16, 256)])
+def test_dz_mode_head_groups_match_one_launch(dt, D):
     # A workspace limit that holds 4 of 6 heads' dZ tiles: the dZ-store mode runs in head
     # groups (fmlp_bwd_plan counts their launches). dX comes from the same dZ tiles and
     # the same GEMM per head, so it is bit-identical to the one-launch result; dW too when
     # the groups split their dW programs as the one launch does; all of it within the
-    # parity bar of the fp32 reference.
+    # parity bar of the fp32 reference. At D = 256 the groups also reuse the H^T region
+    # of the workspace for the D-half-1 GEMM.
     from flashmlp_b200 import _lib
 
-    H, B, D, E = 6, 4096, 128, 1024
+    H, B, E = 6, 4096, 1024
     code = _code(dt)
     L = _lib.lib()
     full = int(L.fmlp_bwd_workspace_size(H, B, D, E, code))
